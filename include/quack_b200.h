@@ -1,0 +1,343 @@
+/*
+ * quack_b200.h -- C ABI of libquack_b200.so: row-reduction kernels for NVIDIA B200 (sm_100a).
+ *
+ * Every entry point takes a pointer to a plain-old-data argument block (raw device pointers,
+ * sizes, strides in ELEMENTS, dtype codes, scalars) and the CUDA stream to launch on.  The
+ * library never allocates or frees device memory, never synchronises the host and keeps no
+ * mutable state between calls apart from per-device, per-kernel attribute caches.  All outputs
+ * and workspaces are allocated and owned by the caller.  A call returns QB_OK (0) once the
+ * kernels are enqueued, or a negative qb_status; qb_last_error() then returns a thread-local,
+ * human readable message.  No entry point aborts the process.
+ *
+ * The entry points replace the TVM-FFI packed functions that the reference (QuACK 0.6.1) builds
+ * with cute.compile(..., "--enable-tvm-ffi") and calls from its torch.library op bodies; the
+ * reference interface each one stands in for is cited at its declaration (paths are relative to
+ * the reference project).
+ */
+#ifndef QUACK_B200_H_
+#define QUACK_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QB_ABI_VERSION 1
+
+/* element types of streamed tensors */
+enum qb_dtype { QB_F32 = 0, QB_F16 = 1, QB_BF16 = 2 };
+/* integer types of class-index tensors */
+enum qb_itype { QB_I32 = 0, QB_I64 = 1 };
+
+enum qb_status {
+  QB_OK = 0,
+  QB_ERR_INVALID = -1,     /* malformed arguments (null pointer, bad dtype, bad size) */
+  QB_ERR_UNSUPPORTED = -2, /* legal request the kernels cannot serve (e.g. row too long) */
+  QB_ERR_CUDA = -3         /* the CUDA runtime reported an error while launching */
+};
+
+/* Opaque CUDA stream handle (cudaStream_t). */
+typedef struct CUstream_st* qb_stream_t;
+
+/*
+ * Optional launch overrides; all-zero selects the built-in sm_100a heuristics.  Plays the role of
+ * the reference's RmsNormFwdConfig / RmsNormBwdConfig (quack/rmsnorm_config.py:16-26,94-107).
+ */
+typedef struct qb_launch_cfg {
+  int32_t num_threads;     /* threads per CTA (power of two, 32..1024) */
+  int32_t threads_per_row; /* threads cooperating on one row inside a CTA (power of two) */
+  int32_t cluster_n;       /* CTAs of a thread-block cluster that share one row (1,2,4,8,16) */
+  int32_t max_ctas;        /* cap on the grid (persistent kernels); 0 = heuristic */
+  int32_t stages;          /* shared-memory prefetch stages (norm backward); 0 = heuristic */
+  int32_t reserved[3];
+} qb_launch_cfg;
+
+/* Device facts the host side needs for workspace sizing. */
+typedef struct qb_device_info {
+  int32_t device;
+  int32_t sm_count;
+  int32_t cc_major;
+  int32_t cc_minor;
+  int32_t max_smem_optin; /* bytes */
+  int32_t max_cluster;    /* largest cluster_n the library will use */
+  int32_t reserved[2];
+} qb_device_info;
+
+/*
+ * RMSNorm / LayerNorm forward.
+ * Replaces the compiled RMSNorm kernel called by quack::_rmsnorm_fwd (quack/rmsnorm.py:365-423,
+ * kernel quack/rmsnorm.py:150-362).
+ *   h = x (+ residual)                      (fp32)
+ *   residual_out = h                        (if residual_out != NULL)
+ *   RMSNorm:   rstd = rsqrt(mean(h^2) + eps);            out = h * rstd * (w + weight_offset) + b
+ *   LayerNorm: mean = mean(h); rstd = rsqrt(var(h)+eps); out = (h - mean) * rstd * (w + off) + b
+ * x/out/residual/residual_out are (M*H, N) matrices with unit column stride and the given row
+ * strides; weight/bias are (H, N) contiguous (H = 1 for the ordinary per-feature case) and may be
+ * NULL; rstd/mean are (M*H) fp32 and may be NULL.  Row r uses head r % H.
+ */
+typedef struct qb_norm_fwd_args {
+  const void* x;
+  const void* weight;
+  const void* bias;
+  const void* residual;
+  void* out;
+  void* residual_out;
+  float* rstd;
+  float* mean;
+  int64_t M;
+  int64_t H;
+  int64_t N;
+  int64_t x_row_stride;
+  int64_t residual_row_stride;
+  int64_t out_row_stride;
+  int64_t residual_out_row_stride;
+  int32_t x_dtype;
+  int32_t weight_dtype;
+  int32_t bias_dtype;
+  int32_t residual_dtype;
+  int32_t out_dtype;
+  int32_t residual_out_dtype;
+  int32_t is_layernorm;
+  float eps;
+  float weight_offset;
+  int32_t pad0;
+  qb_launch_cfg cfg;
+} qb_norm_fwd_args;
+
+int qb_norm_fwd(const qb_norm_fwd_args* args, qb_stream_t stream);
+
+/*
+ * RMSNorm / LayerNorm backward, stage 1 (persistent kernel).
+ * Replaces the compiled RMSNormBackward kernel called by quack::_rmsnorm_bwd
+ * (quack/rmsnorm.py:1208-1286, kernel quack/rmsnorm.py:723-1205).
+ *   xhat = (x - mean) * rstd   (mean = 0 for RMSNorm)
+ *   wdy  = dout * (w + weight_offset)
+ *   dx   = (wdy - xhat * mean(xhat*wdy) [- mean(wdy) for LayerNorm]) * rstd (+ dresidual_out)
+ *   dresidual = dx                      (written only if dresidual != NULL; own dtype)
+ *   dw_partial[p, h, :] = sum over the rows CTA p handled of dout * xhat   (fp32)
+ *   db_partial[p, h, :] = sum over the rows CTA p handled of dout          (fp32)
+ * num_partials (P) is the first dimension of dw_partial / db_partial and fixes the number of
+ * row-owning CTAs (times cluster_n CTAs each); every one of the P*H slices is fully written even
+ * if its CTA handled no row, so the workspaces need no initialisation.
+ */
+typedef struct qb_norm_bwd_args {
+  const void* x;
+  const void* weight;
+  const void* dout;
+  const float* rstd;
+  const float* mean; /* required iff is_layernorm */
+  const void* dresidual_out;
+  void* dx;
+  void* dresidual;
+  float* dw_partial;
+  float* db_partial;
+  int64_t M;
+  int64_t H;
+  int64_t N;
+  int64_t x_row_stride;
+  int64_t dout_row_stride;
+  int64_t dresidual_out_row_stride;
+  int64_t dx_row_stride;
+  int64_t dresidual_row_stride;
+  int32_t num_partials;
+  int32_t x_dtype;
+  int32_t weight_dtype;
+  int32_t dout_dtype;
+  int32_t dresidual_out_dtype;
+  int32_t dx_dtype;
+  int32_t dresidual_dtype;
+  int32_t is_layernorm;
+  float weight_offset;
+  int32_t pad0;
+  qb_launch_cfg cfg;
+} qb_norm_bwd_args;
+
+int qb_norm_bwd(const qb_norm_bwd_args* args, qb_stream_t stream);
+
+/*
+ * Number of partial-sum slices (P) the backward heuristics want for a row length, i.e. the first
+ * dimension of dw_partial.  Replaces get_sm_count (quack/rmsnorm_config.py:265-293).
+ */
+int qb_norm_bwd_num_partials(int64_t N, int32_t x_dtype, int32_t is_layernorm, int32_t device);
+
+/*
+ * Norm backward, stage 2: deterministic fixed-order reduction of the fp32 partials over P and
+ * cast to the parameter dtype.  Replaces `dw_partial.sum(dim=0).to(weight.dtype)`
+ * (quack/rmsnorm.py:1398-1399, 1719-1720).  partial is (P, cols) fp32 contiguous; out is (cols).
+ * If out_f32 != NULL the fp32 sum is also stored there (used before a cross-GPU all-reduce so
+ * that every rank rounds the same global sum).  Either output may be NULL.
+ */
+typedef struct qb_colsum_args {
+  const float* partial;
+  void* out;
+  float* out_f32;
+  int64_t P;
+  int64_t cols;
+  int32_t out_dtype;
+  int32_t pad0;
+} qb_colsum_args;
+
+int qb_colsum(const qb_colsum_args* args, qb_stream_t stream);
+
+/*
+ * Softmax forward over the last dimension of an (M, N) matrix.
+ * Replaces the compiled Softmax kernel called by quack::_softmax_fwd (quack/softmax.py:193-207,
+ * kernel quack/softmax.py:87-176).
+ */
+typedef struct qb_softmax_fwd_args {
+  const void* x;
+  void* out;
+  int64_t M;
+  int64_t N;
+  int64_t x_row_stride;
+  int64_t out_row_stride;
+  int32_t x_dtype;
+  int32_t out_dtype;
+  qb_launch_cfg cfg;
+} qb_softmax_fwd_args;
+
+int qb_softmax_fwd(const qb_softmax_fwd_args* args, qb_stream_t stream);
+
+/*
+ * Softmax backward: dx = y * (dy - sum(dy * y)).
+ * Replaces the compiled SoftmaxBackward kernel called by quack::_softmax_backward
+ * (quack/softmax.py:373-391, kernel quack/softmax.py:275-353).
+ */
+typedef struct qb_softmax_bwd_args {
+  const void* dy;
+  const void* y;
+  void* dx;
+  int64_t M;
+  int64_t N;
+  int64_t dy_row_stride;
+  int64_t y_row_stride;
+  int64_t dx_row_stride;
+  int32_t dy_dtype;
+  int32_t y_dtype;
+  int32_t dx_dtype;
+  int32_t pad0;
+  qb_launch_cfg cfg;
+} qb_softmax_bwd_args;
+
+int qb_softmax_bwd(const qb_softmax_bwd_args* args, qb_stream_t stream);
+
+/*
+ * Cross-entropy forward (optionally also the gradient w.r.t. the logits).
+ * Replaces the compiled CrossEntropy kernel called by quack::cross_entropy_fwd_out
+ * (quack/cross_entropy.py:312-364, kernel quack/cross_entropy.py:113-265).
+ *   lse[r]  = log(sum_j exp(x[r, j]))
+ *   loss[r] = w[t] * (lse[r] - tl[r])          or exactly 0 if t == ignore_index
+ *     where t = target[r] and tl[r] = x[r, t], or target_logit[r, t] / target_logit[r] if given
+ *   dx[r,:] = w[t] * (softmax(x[r,:]) - onehot(t))   or exactly 0 if t == ignore_index
+ * Sharded use (vocabulary split over GPUs): if row_max / row_sumexp / row_tgt are given the
+ * kernel stores, per row, max_j x, sum_j exp(x - max) and the raw target logit (0 when the
+ * target column is outside [col_offset, col_offset + N) or ignored), and loss / lse may be NULL.
+ * target holds GLOBAL class ids; col_offset is the id of this shard's first column.
+ * dx may alias x (in-place).
+ */
+typedef struct qb_ce_fwd_args {
+  const void* x;
+  const void* target;
+  const void* target_logit; /* optional */
+  const void* weight;       /* optional per-class weights, indexed by global class id */
+  float* loss;              /* optional when the row_* outputs are given */
+  float* lse;               /* optional */
+  void* dx;                 /* optional */
+  float* row_max;           /* optional (sharded) */
+  float* row_sumexp;        /* optional (sharded) */
+  float* row_tgt;           /* optional (sharded) */
+  int64_t M;
+  int64_t N;
+  int64_t x_row_stride;
+  int64_t dx_row_stride;
+  int64_t target_logit_row_stride; /* elements; used when target_logit_ndim == 2 */
+  int64_t col_offset;
+  int64_t ignore_index;
+  int32_t x_dtype;
+  int32_t target_dtype; /* qb_itype */
+  int32_t target_logit_dtype;
+  int32_t target_logit_ndim; /* 1 or 2 */
+  int32_t weight_dtype;
+  int32_t pad0;
+  qb_launch_cfg cfg;
+} qb_ce_fwd_args;
+
+int qb_ce_fwd(const qb_ce_fwd_args* args, qb_stream_t stream);
+
+/*
+ * Cross-entropy backward from a saved log-sum-exp.
+ * Replaces the compiled CrossEntropyBackward kernel called by quack::cross_entropy_bwd_out
+ * (quack/cross_entropy.py:574-628, kernel quack/cross_entropy.py:463-546).
+ *   dx[r, j] = (exp(x[r, j] - lse[r]) - [col_offset + j == target[r]]) * dloss[r] * w[target[r]]
+ * and exactly 0 for rows whose target equals ignore_index.  dloss is read with an element stride
+ * (0 is allowed: one broadcast value).  dx may alias x.
+ */
+typedef struct qb_ce_bwd_args {
+  const void* x;
+  const void* target;
+  const float* dloss;
+  const float* lse;
+  const void* weight; /* optional */
+  void* dx;
+  int64_t M;
+  int64_t N;
+  int64_t x_row_stride;
+  int64_t dx_row_stride;
+  int64_t dloss_stride;
+  int64_t col_offset;
+  int64_t ignore_index;
+  int32_t x_dtype;
+  int32_t dx_dtype;
+  int32_t target_dtype;
+  int32_t weight_dtype;
+  qb_launch_cfg cfg;
+} qb_ce_bwd_args;
+
+int qb_ce_bwd(const qb_ce_bwd_args* args, qb_stream_t stream);
+
+/*
+ * Vocabulary-sharded cross-entropy, combine step.  The reference has no multi-GPU path; its
+ * single-GPU analogue is the lse_partial mode of CrossEntropyFunction
+ * (quack/cross_entropy.py:676-694).  stats is (G, 3, M) fp32: for each shard g the per-row
+ * max, sum-exp (relative to that max) and raw target logit, gathered in rank order.  Computes, in
+ * fixed shard order, m = max_g m_g, s = sum_g s_g * exp(m_g - m), t = sum_g t_g,
+ * lse = m + log(s), loss = w[target] * (lse - t), or exactly 0 for ignored rows.
+ */
+typedef struct qb_ce_combine_args {
+  const float* stats;
+  const void* target;
+  const void* weight; /* optional */
+  float* loss;
+  float* lse;
+  int64_t G;
+  int64_t M;
+  int64_t ignore_index;
+  int32_t target_dtype;
+  int32_t weight_dtype;
+} qb_ce_combine_args;
+
+int qb_ce_combine(const qb_ce_combine_args* args, qb_stream_t stream);
+
+/* Fills *info for a CUDA device ordinal (-1 = current device). */
+int qb_query_device(int32_t device, qb_device_info* info);
+
+/* Message of the last failing call made by this thread ("" if none). */
+const char* qb_last_error(void);
+
+/* ABI self-description: QB_ABI_VERSION the library was built with. */
+int qb_abi_version(void);
+
+/*
+ * sizeof() of an argument block as compiled into the library, so a foreign-language binding can
+ * verify its struct layout before the first call.  which: 0 launch_cfg, 1 norm_fwd, 2 norm_bwd,
+ * 3 colsum, 4 softmax_fwd, 5 softmax_bwd, 6 ce_fwd, 7 ce_bwd, 8 ce_combine, 9 device_info.
+ * Returns -1 for an unknown code.
+ */
+int qb_sizeof_args(int32_t which);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* QUACK_B200_H_ */

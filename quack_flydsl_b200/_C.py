@@ -1,0 +1,300 @@
+"""ctypes binding of libquack_b200.so (declared in include/quack_b200.h).
+
+Plays the role of the TVM-FFI call boundary in the reference (the compiled functions invoked from
+quack/rmsnorm.py:423, quack/softmax.py:207, quack/cross_entropy.py:364): tensors cross as raw
+device pointers + sizes + strides, the stream is torch's current stream.  There is no fallback:
+if the library is missing or a call fails, an exception is raised.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import POINTER, Structure, byref, c_char_p, c_float, c_int32, c_int64, c_void_p
+from pathlib import Path
+from typing import Optional
+
+import torch
+
+QB_F32, QB_F16, QB_BF16 = 0, 1, 2
+QB_I32, QB_I64 = 0, 1
+QB_OK, QB_ERR_INVALID, QB_ERR_UNSUPPORTED, QB_ERR_CUDA = 0, -1, -2, -3
+QB_ABI_VERSION = 1
+
+FLOAT_CODES = {torch.float32: QB_F32, torch.float16: QB_F16, torch.bfloat16: QB_BF16}
+INDEX_CODES = {torch.int32: QB_I32, torch.int64: QB_I64}
+
+
+class LaunchCfg(Structure):
+    _fields_ = [
+        ("num_threads", c_int32),
+        ("threads_per_row", c_int32),
+        ("cluster_n", c_int32),
+        ("max_ctas", c_int32),
+        ("stages", c_int32),
+        ("reserved", c_int32 * 3),
+    ]
+
+
+class DeviceInfo(Structure):
+    _fields_ = [
+        ("device", c_int32),
+        ("sm_count", c_int32),
+        ("cc_major", c_int32),
+        ("cc_minor", c_int32),
+        ("max_smem_optin", c_int32),
+        ("max_cluster", c_int32),
+        ("reserved", c_int32 * 2),
+    ]
+
+
+class NormFwdArgs(Structure):
+    _fields_ = [
+        ("x", c_void_p), ("weight", c_void_p), ("bias", c_void_p), ("residual", c_void_p),
+        ("out", c_void_p), ("residual_out", c_void_p), ("rstd", c_void_p), ("mean", c_void_p),
+        ("M", c_int64), ("H", c_int64), ("N", c_int64),
+        ("x_row_stride", c_int64), ("residual_row_stride", c_int64),
+        ("out_row_stride", c_int64), ("residual_out_row_stride", c_int64),
+        ("x_dtype", c_int32), ("weight_dtype", c_int32), ("bias_dtype", c_int32),
+        ("residual_dtype", c_int32), ("out_dtype", c_int32), ("residual_out_dtype", c_int32),
+        ("is_layernorm", c_int32), ("eps", c_float), ("weight_offset", c_float),
+        ("pad0", c_int32), ("cfg", LaunchCfg),
+    ]
+
+
+class NormBwdArgs(Structure):
+    _fields_ = [
+        ("x", c_void_p), ("weight", c_void_p), ("dout", c_void_p), ("rstd", c_void_p),
+        ("mean", c_void_p), ("dresidual_out", c_void_p), ("dx", c_void_p),
+        ("dresidual", c_void_p), ("dw_partial", c_void_p), ("db_partial", c_void_p),
+        ("M", c_int64), ("H", c_int64), ("N", c_int64),
+        ("x_row_stride", c_int64), ("dout_row_stride", c_int64),
+        ("dresidual_out_row_stride", c_int64), ("dx_row_stride", c_int64),
+        ("dresidual_row_stride", c_int64),
+        ("num_partials", c_int32), ("x_dtype", c_int32), ("weight_dtype", c_int32),
+        ("dout_dtype", c_int32), ("dresidual_out_dtype", c_int32), ("dx_dtype", c_int32),
+        ("dresidual_dtype", c_int32), ("is_layernorm", c_int32), ("weight_offset", c_float),
+        ("pad0", c_int32), ("cfg", LaunchCfg),
+    ]
+
+
+class ColsumArgs(Structure):
+    _fields_ = [
+        ("partial", c_void_p), ("out", c_void_p), ("out_f32", c_void_p),
+        ("P", c_int64), ("cols", c_int64), ("out_dtype", c_int32), ("pad0", c_int32),
+    ]
+
+
+class SoftmaxFwdArgs(Structure):
+    _fields_ = [
+        ("x", c_void_p), ("out", c_void_p), ("M", c_int64), ("N", c_int64),
+        ("x_row_stride", c_int64), ("out_row_stride", c_int64),
+        ("x_dtype", c_int32), ("out_dtype", c_int32), ("cfg", LaunchCfg),
+    ]
+
+
+class SoftmaxBwdArgs(Structure):
+    _fields_ = [
+        ("dy", c_void_p), ("y", c_void_p), ("dx", c_void_p), ("M", c_int64), ("N", c_int64),
+        ("dy_row_stride", c_int64), ("y_row_stride", c_int64), ("dx_row_stride", c_int64),
+        ("dy_dtype", c_int32), ("y_dtype", c_int32), ("dx_dtype", c_int32), ("pad0", c_int32),
+        ("cfg", LaunchCfg),
+    ]
+
+
+class CeFwdArgs(Structure):
+    _fields_ = [
+        ("x", c_void_p), ("target", c_void_p), ("target_logit", c_void_p), ("weight", c_void_p),
+        ("loss", c_void_p), ("lse", c_void_p), ("dx", c_void_p),
+        ("row_max", c_void_p), ("row_sumexp", c_void_p), ("row_tgt", c_void_p),
+        ("M", c_int64), ("N", c_int64), ("x_row_stride", c_int64), ("dx_row_stride", c_int64),
+        ("target_logit_row_stride", c_int64), ("col_offset", c_int64), ("ignore_index", c_int64),
+        ("x_dtype", c_int32), ("target_dtype", c_int32), ("target_logit_dtype", c_int32),
+        ("target_logit_ndim", c_int32), ("weight_dtype", c_int32), ("pad0", c_int32),
+        ("cfg", LaunchCfg),
+    ]
+
+
+class CeBwdArgs(Structure):
+    _fields_ = [
+        ("x", c_void_p), ("target", c_void_p), ("dloss", c_void_p), ("lse", c_void_p),
+        ("weight", c_void_p), ("dx", c_void_p),
+        ("M", c_int64), ("N", c_int64), ("x_row_stride", c_int64), ("dx_row_stride", c_int64),
+        ("dloss_stride", c_int64), ("col_offset", c_int64), ("ignore_index", c_int64),
+        ("x_dtype", c_int32), ("dx_dtype", c_int32), ("target_dtype", c_int32),
+        ("weight_dtype", c_int32), ("cfg", LaunchCfg),
+    ]
+
+
+class CeCombineArgs(Structure):
+    _fields_ = [
+        ("stats", c_void_p), ("target", c_void_p), ("weight", c_void_p),
+        ("loss", c_void_p), ("lse", c_void_p),
+        ("G", c_int64), ("M", c_int64), ("ignore_index", c_int64),
+        ("target_dtype", c_int32), ("weight_dtype", c_int32),
+    ]
+
+
+# code passed to qb_sizeof_args -> the Structure that must have that size
+_SIZEOF_CODES = {
+    0: LaunchCfg, 1: NormFwdArgs, 2: NormBwdArgs, 3: ColsumArgs, 4: SoftmaxFwdArgs,
+    5: SoftmaxBwdArgs, 6: CeFwdArgs, 7: CeBwdArgs, 8: CeCombineArgs, 9: DeviceInfo,
+}
+
+# every symbol include/quack_b200.h declares
+EXPORTED_SYMBOLS = (
+    "qb_norm_fwd", "qb_norm_bwd", "qb_norm_bwd_num_partials", "qb_colsum", "qb_softmax_fwd",
+    "qb_softmax_bwd", "qb_ce_fwd", "qb_ce_bwd", "qb_ce_combine", "qb_query_device",
+    "qb_last_error", "qb_abi_version", "qb_sizeof_args",
+)
+
+_LIB: Optional[ctypes.CDLL] = None
+
+
+def library_path() -> Path:
+    """Location of the shared library (override with QUACK_B200_LIB for an experimental build)."""
+    override = os.environ.get("QUACK_B200_LIB")
+    if override:
+        return Path(override)
+    return Path(__file__).resolve().parent / "lib" / "libquack_b200.so"
+
+
+def lib() -> ctypes.CDLL:
+    """Loads (once) and returns the CUDA library; raises if it is missing or mismatched."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    path = library_path()
+    if not path.exists():
+        raise ImportError(
+            f"{path} not found: the sm_100a kernels are not built. Run "
+            "`python -m quack_flydsl_b200.build` (needs nvcc). There is no fallback path."
+        )
+    cdll = ctypes.CDLL(str(path))
+    for name in EXPORTED_SYMBOLS:
+        if not hasattr(cdll, name):
+            raise ImportError(f"{path} does not export {name}")
+    cdll.qb_last_error.restype = c_char_p
+    cdll.qb_last_error.argtypes = []
+    cdll.qb_abi_version.restype = ctypes.c_int
+    cdll.qb_sizeof_args.restype = ctypes.c_int
+    cdll.qb_sizeof_args.argtypes = [c_int32]
+    if cdll.qb_abi_version() != QB_ABI_VERSION:
+        raise ImportError(f"{path}: ABI version {cdll.qb_abi_version()} != {QB_ABI_VERSION}")
+    for code, struct in _SIZEOF_CODES.items():
+        want = cdll.qb_sizeof_args(code)
+        if want != ctypes.sizeof(struct):
+            raise ImportError(
+                f"{path}: layout mismatch for {struct.__name__}: library {want} bytes, "
+                f"binding {ctypes.sizeof(struct)} bytes"
+            )
+    for name, struct in (
+        ("qb_norm_fwd", NormFwdArgs), ("qb_norm_bwd", NormBwdArgs), ("qb_colsum", ColsumArgs),
+        ("qb_softmax_fwd", SoftmaxFwdArgs), ("qb_softmax_bwd", SoftmaxBwdArgs),
+        ("qb_ce_fwd", CeFwdArgs), ("qb_ce_bwd", CeBwdArgs), ("qb_ce_combine", CeCombineArgs),
+    ):
+        fn = getattr(cdll, name)
+        fn.restype = ctypes.c_int
+        fn.argtypes = [POINTER(struct), c_void_p]
+    cdll.qb_norm_bwd_num_partials.restype = ctypes.c_int
+    cdll.qb_norm_bwd_num_partials.argtypes = [c_int64, c_int32, c_int32, c_int32]
+    cdll.qb_query_device.restype = ctypes.c_int
+    cdll.qb_query_device.argtypes = [c_int32, POINTER(DeviceInfo)]
+    _LIB = cdll
+    return cdll
+
+
+def last_error() -> str:
+    return lib().qb_last_error().decode("utf-8", "replace")
+
+
+def check(status: int, what: str) -> None:
+    """Turns a negative qb_status into the exception type the reference raises for that case."""
+    if status == QB_OK:
+        return
+    msg = f"{what}: {last_error()}"
+    if status in (QB_ERR_INVALID, QB_ERR_UNSUPPORTED):
+        raise ValueError(msg)
+    raise RuntimeError(msg)
+
+
+def float_code(t: Optional[torch.Tensor]) -> int:
+    return FLOAT_CODES[t.dtype] if t is not None else 0
+
+
+def ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return t.data_ptr() if t is not None else None
+
+
+def make_cfg(num_threads: int = 0, threads_per_row: int = 0, cluster_n: int = 0,
+             max_ctas: int = 0, stages: int = 0) -> LaunchCfg:
+    cfg = LaunchCfg()
+    cfg.num_threads = int(num_threads)
+    cfg.threads_per_row = int(threads_per_row)
+    cfg.cluster_n = int(cluster_n)
+    cfg.max_ctas = int(max_ctas)
+    cfg.stages = int(stages)
+    return cfg
+
+
+def env_cfg(op: str) -> Optional[LaunchCfg]:
+    """Launch override from QUACK_B200_CFG="op:threads:threads_per_row:cluster:max_ctas:stages;..."
+    (used by tuning sweeps; 0 keeps the heuristic for a field)."""
+    spec = os.environ.get("QUACK_B200_CFG")
+    if not spec:
+        return None
+    for item in spec.split(";"):
+        parts = item.split(":")
+        if parts and parts[0] == op:
+            vals = [int(v) if v else 0 for v in parts[1:6]]
+            vals += [0] * (5 - len(vals))
+            return make_cfg(*vals)
+    return None
+
+
+def require_cuda(t: torch.Tensor, name: str) -> None:
+    # Same wording as the TVM-FFI check the reference relies on (tests/test_rmsnorm.py:364).
+    if t.device.type != "cuda":
+        raise ValueError(
+            f"Mismatched Tensor on argument {name}: expected device_type=cuda, got {t.device.type}"
+        )
+
+
+def stream_of(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+class device_of:
+    """Makes the tensor's device current for the duration of a launch (no-op if it already is)."""
+
+    def __init__(self, t: torch.Tensor):
+        self.idx = t.device.index if t.device.index is not None else torch.cuda.current_device()
+        self.prev = None
+
+    def __enter__(self):
+        cur = torch.cuda.current_device()
+        if cur != self.idx:
+            self.prev = cur
+            torch.cuda.set_device(self.idx)
+        return self
+
+    def __exit__(self, *exc):
+        if self.prev is not None:
+            torch.cuda.set_device(self.prev)
+        return False
+
+
+def query_device(device: int = -1) -> DeviceInfo:
+    info = DeviceInfo()
+    check(lib().qb_query_device(device, byref(info)), "qb_query_device")
+    return info
+
+
+def norm_bwd_num_partials(N: int, x_dtype: torch.dtype, is_layernorm: bool, device) -> int:
+    dev = torch.device(device)
+    with torch.cuda.device(dev):
+        n = lib().qb_norm_bwd_num_partials(int(N), FLOAT_CODES[x_dtype], int(is_layernorm),
+                                           dev.index if dev.index is not None else -1)
+    if n <= 0:
+        check(n if n < 0 else QB_ERR_INVALID, "qb_norm_bwd_num_partials")
+    return n

@@ -1,0 +1,105 @@
+// Library-level entry points: error string, device query, ABI self-description.
+#include <mutex>
+#include <string.h>
+
+#include "host_common.h"
+
+namespace qb {
+
+static thread_local char g_error[512] = "";
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_error, sizeof(g_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+void clear_error() { g_error[0] = '\0'; }
+
+static constexpr int kMaxDevices = 64;
+static DeviceFacts g_facts[kMaxDevices];
+static bool g_facts_ready[kMaxDevices];
+static std::mutex g_facts_mutex;
+
+static const DeviceFacts* device_facts(int device) {
+  if (device < 0 || device >= kMaxDevices) {
+    set_error(QB_ERR_INVALID, "device ordinal %d out of range", device);
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_facts_mutex);
+  if (!g_facts_ready[device]) {
+    DeviceFacts f;
+    f.device = device;
+    cudaError_t e = cudaDeviceGetAttribute(&f.sm_count, cudaDevAttrMultiProcessorCount, device);
+    if (e == cudaSuccess)
+      e = cudaDeviceGetAttribute(&f.cc_major, cudaDevAttrComputeCapabilityMajor, device);
+    if (e == cudaSuccess)
+      e = cudaDeviceGetAttribute(&f.cc_minor, cudaDevAttrComputeCapabilityMinor, device);
+    if (e == cudaSuccess)
+      e = cudaDeviceGetAttribute(&f.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+    if (e != cudaSuccess) {
+      set_error(QB_ERR_CUDA, "cudaDeviceGetAttribute(device %d): %s", device, cudaGetErrorString(e));
+      return nullptr;
+    }
+    if (f.cc_major < 10) {
+      set_error(QB_ERR_UNSUPPORTED,
+                "device %d has compute capability %d.%d; this library is built for sm_100a only",
+                device, f.cc_major, f.cc_minor);
+      return nullptr;
+    }
+    g_facts[device] = f;
+    g_facts_ready[device] = true;
+  }
+  return &g_facts[device];
+}
+
+const DeviceFacts* current_device_facts() {
+  int device = -1;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) {
+    set_error(QB_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+    return nullptr;
+  }
+  return device_facts(device);
+}
+
+}  // namespace qb
+
+using namespace qb;
+
+extern "C" int qb_query_device(int32_t device, qb_device_info* info) {
+  clear_error();
+  if (info == nullptr) return set_error(QB_ERR_INVALID, "query_device: null info");
+  const DeviceFacts* f = device < 0 ? current_device_facts() : device_facts(device);
+  if (f == nullptr) return g_error[0] && strstr(g_error, "built for") ? QB_ERR_UNSUPPORTED : QB_ERR_CUDA;
+  memset(info, 0, sizeof(*info));
+  info->device = f->device;
+  info->sm_count = f->sm_count;
+  info->cc_major = f->cc_major;
+  info->cc_minor = f->cc_minor;
+  info->max_smem_optin = f->max_smem_optin;
+  info->max_cluster = 16;
+  return QB_OK;
+}
+
+extern "C" const char* qb_last_error(void) { return g_error; }
+
+extern "C" int qb_abi_version(void) { return QB_ABI_VERSION; }
+
+extern "C" int qb_sizeof_args(int32_t which) {
+  switch (which) {
+    case 0: return (int)sizeof(qb_launch_cfg);
+    case 1: return (int)sizeof(qb_norm_fwd_args);
+    case 2: return (int)sizeof(qb_norm_bwd_args);
+    case 3: return (int)sizeof(qb_colsum_args);
+    case 4: return (int)sizeof(qb_softmax_fwd_args);
+    case 5: return (int)sizeof(qb_softmax_bwd_args);
+    case 6: return (int)sizeof(qb_ce_fwd_args);
+    case 7: return (int)sizeof(qb_ce_bwd_args);
+    case 8: return (int)sizeof(qb_ce_combine_args);
+    case 9: return (int)sizeof(qb_device_info);
+    default: return -1;
+  }
+}

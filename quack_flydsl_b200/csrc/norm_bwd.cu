@@ -1,0 +1,503 @@
+// RMSNorm / LayerNorm backward for sm_100a: persistent stage-1 kernel and the deterministic
+// stage-2 column sum.
+//
+// Stage 1 follows quack/rmsnorm.py:723-1205 (RMSNormBackward.kernel): a fixed grid of P CTAs (or
+// clusters) walks the rows with stride P, keeps fp32 dw / db accumulators for its columns in
+// registers for the whole launch and finally writes them as row p of the [P, N] partial buffers.
+// x, dout (and dresidual_out) of the next rows are prefetched into shared memory with cp.async
+// through a multi-stage ring; every thread reads back only the bytes it copied itself, so the
+// ring needs no barriers.  Stage 2 replaces the reference's `dw_partial.sum(dim=0)`
+// (quack/rmsnorm.py:1398-1399) by a fixed-order tree, so dw / db are bit-reproducible.
+#include "common.cuh"
+#include "host_common.h"
+
+namespace qb {
+
+struct NormBwdParams {
+  qb_norm_bwd_args a;
+  int tpr;
+  int rows_per_cta;
+  int cluster_n;
+  int cols_per_cta;
+  int64_t num_tiles;
+  int stages;  // shared-memory ring depth (>= 1)
+  int n_in;    // streamed inputs per row: 2 (x, dout) or 3 (+ dresidual_out)
+};
+
+constexpr int kMaxStages = 8;
+
+__device__ __forceinline__ void cp_async_wait_dyn(int n) {
+  switch (n) {
+    case 0: cp_async_wait<0>(); break;
+    case 1: cp_async_wait<1>(); break;
+    case 2: cp_async_wait<2>(); break;
+    case 3: cp_async_wait<3>(); break;
+    case 4: cp_async_wait<4>(); break;
+    case 5: cp_async_wait<5>(); break;
+    case 6: cp_async_wait<6>(); break;
+    default: cp_async_wait<7>(); break;
+  }
+}
+
+// DT: dtype shared by x / dout / dx (/ dresidual_out / dresidual) or kDynDT.
+// LN: LayerNorm (mean subtraction, second row statistic).  DB: accumulate db.
+template <int DT, int VEC, int K, bool LN, bool DB>
+__global__ void __launch_bounds__((K * VEC <= 8) ? 1024 : ((K * VEC <= 16) ? 512 : 256))
+norm_bwd_kernel(const NormBwdParams p) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ ReduceScratch scratch;
+  const qb_norm_bwd_args& a = p.a;
+  const RowGeom g = make_geom(p.tpr, p.cluster_n);
+  if (p.cluster_n > 1) cluster_arrive();
+
+  constexpr int kSlot = RawWords<DT, VEC>::value * 4;  // bytes of one staged chunk
+  const int N = static_cast<int>(a.N);
+  const int h = blockIdx.y;
+  const int nthreads = blockDim.x;
+  const int col0 = static_cast<int>(g.crank) * p.cols_per_cta;
+  const int ncols = min(p.cols_per_cta, N - col0);
+  const float inv_n = 1.0f / static_cast<float>(N);
+  const bool has_dres_out = a.dresidual_out != nullptr;
+
+  int col[K];
+  bool cok[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const int local = (k * p.tpr + g.t) * VEC;
+    cok[k] = local < ncols;
+    col[k] = col0 + local;
+  }
+
+  // Weight (+ offset) for this thread's columns, fp32, held for the whole launch.
+  float w[K][VEC];
+  const int64_t wrow = static_cast<int64_t>(h) * N;
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    if (a.weight != nullptr) {
+      load_chunk<kDynDT, VEC, false>(w[k], a.weight, wrow + col[k], a.weight_dtype, cok[k]);
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) w[k][i] += a.weight_offset;
+    } else {
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) w[k][i] = 1.0f;
+    }
+  }
+  float dw[K][VEC];
+  float db[DB ? K : 1][VEC];
+#pragma unroll
+  for (int k = 0; k < K; ++k)
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      dw[k][i] = 0.0f;
+      if constexpr (DB) db[k][i] = 0.0f;
+    }
+
+  // Shared-memory ring: stage s, input j, chunk k, thread tid -> one slot of kSlot bytes.
+  const int64_t P = gridDim.x / p.cluster_n;
+  const int64_t pidx = blockIdx.x / p.cluster_n;
+  const size_t stage_bytes = static_cast<size_t>(p.n_in) * K * nthreads * kSlot;
+  auto slot_ptr = [&](int stage, int j, int k) -> unsigned char* {
+    return smem_raw + stage * stage_bytes +
+           (static_cast<size_t>(j * K + k) * nthreads + threadIdx.x) * kSlot;
+  };
+  auto issue_tile = [&](int64_t tile, int stage) {
+    if (tile < p.num_tiles) {
+      const int64_t m = tile * p.rows_per_cta + g.r;
+      if (m < a.M) {
+        const int64_t row = m * a.H + h;
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+          if (cok[k]) {
+            stage_chunk<DT, VEC>(slot_ptr(stage, 0, k), a.x, row * a.x_row_stride + col[k],
+                                 a.x_dtype);
+            stage_chunk<DT, VEC>(slot_ptr(stage, 1, k), a.dout, row * a.dout_row_stride + col[k],
+                                 a.dout_dtype);
+            if (has_dres_out)
+              stage_chunk<DT, VEC>(slot_ptr(stage, 2, k), a.dresidual_out,
+                                   row * a.dresidual_out_row_stride + col[k],
+                                   a.dresidual_out_dtype);
+          }
+        }
+      }
+    }
+    cp_async_commit();  // one group per tile slot, possibly empty
+  };
+
+  const int S = p.stages;
+  for (int s = 0; s < S - 1; ++s) issue_tile(pidx + s * P, s);
+
+  // Row statistics of the first tile; the next tile's are fetched one iteration ahead.
+  float rstd_nx = 0.0f, mean_nx = 0.0f;
+  {
+    const int64_t m = pidx * p.rows_per_cta + g.r;
+    if (pidx < p.num_tiles && m < a.M) {
+      rstd_nx = a.rstd[m * a.H + h];
+      if constexpr (LN) mean_nx = a.mean[m * a.H + h];
+    }
+  }
+
+  int parity = 0;
+  bool first = true;
+  int it = 0;
+  for (int64_t tile = pidx; tile < p.num_tiles; tile += P, ++it) {
+    issue_tile(tile + static_cast<int64_t>(S - 1) * P, (it + S - 1) % S);
+    const int stage = it % S;
+    const int64_t m = tile * p.rows_per_cta + g.r;
+    const bool row_ok = m < a.M;
+    const int64_t row = m * a.H + h;
+    const float rstd = rstd_nx;
+    const float mean = mean_nx;
+    {
+      const int64_t mn = (tile + P) * p.rows_per_cta + g.r;
+      if (tile + P < p.num_tiles && mn < a.M) {
+        rstd_nx = a.rstd[mn * a.H + h];
+        if constexpr (LN) mean_nx = a.mean[mn * a.H + h];
+      }
+    }
+    cp_async_wait_dyn(S - 1);  // this tile's group has landed; S-1 younger groups may be in flight
+
+    // ---- pass 1: row statistics c1 = mean(xhat * wdy), c2 = mean(wdy) ----
+    float s1 = 0.0f, s2 = 0.0f;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      if (row_ok && cok[k]) {
+        float x[VEC], dy[VEC];
+        load_chunk_smem<DT, VEC>(x, slot_ptr(stage, 0, k), a.x_dtype);
+        load_chunk_smem<DT, VEC>(dy, slot_ptr(stage, 1, k), a.dout_dtype);
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) {
+          const float xhat = (LN ? (x[i] - mean) : x[i]) * rstd;
+          const float wdy = dy[i] * w[k][i];
+          s1 = fmaf(xhat, wdy, s1);
+          if constexpr (LN) s2 += wdy;
+        }
+      }
+    }
+    if (first && p.cluster_n > 1) cluster_wait();
+    first = false;
+    const float2 red = row_reduce<SumOp>(make_float2(s1, s2), g, scratch, 0, parity);
+    parity ^= 1;
+    const float c1 = red.x * inv_n;
+    const float c2 = LN ? red.y * inv_n : 0.0f;
+
+    // ---- pass 2: dx, dresidual, dw / db accumulation ----
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      if (row_ok && cok[k]) {
+        float x[VEC], dy[VEC], dx[VEC];
+        load_chunk_smem<DT, VEC>(x, slot_ptr(stage, 0, k), a.x_dtype);
+        load_chunk_smem<DT, VEC>(dy, slot_ptr(stage, 1, k), a.dout_dtype);
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) {
+          const float xhat = (LN ? (x[i] - mean) : x[i]) * rstd;
+          const float wdy = dy[i] * w[k][i];
+          dx[i] = (wdy - xhat * c1 - c2) * rstd;
+          dw[k][i] = fmaf(dy[i], xhat, dw[k][i]);
+          if constexpr (DB) db[k][i] += dy[i];
+        }
+        if (has_dres_out) {
+          float dr[VEC];
+          load_chunk_smem<DT, VEC>(dr, slot_ptr(stage, 2, k), a.dresidual_out_dtype);
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) dx[i] += dr[i];
+        }
+        store_chunk<DT, VEC>(a.dx, row * a.dx_row_stride + col[k], dx, a.dx_dtype);
+        if (a.dresidual != nullptr)
+          store_chunk<DT, VEC>(a.dresidual, row * a.dresidual_row_stride + col[k], dx,
+                               a.dresidual_dtype);
+      }
+    }
+  }
+  if (first && p.cluster_n > 1) cluster_wait();
+  cp_async_wait<0>();
+
+  // ---- epilogue: this CTA's partial sums -> row pidx of the [P, H, N] workspaces ----
+  const int64_t prow = (pidx * a.H + h) * static_cast<int64_t>(N);
+  if (p.rows_per_cta == 1) {
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      if (cok[k]) {
+        if (a.dw_partial != nullptr)
+          store_chunk<QB_F32, VEC>(a.dw_partial, prow + col[k], dw[k], QB_F32);
+        if constexpr (DB) {
+          if (a.db_partial != nullptr)
+            store_chunk<QB_F32, VEC>(a.db_partial, prow + col[k], db[k], QB_F32);
+        }
+      }
+    }
+  } else {
+    // Several rows per CTA tile: fold the row groups in fixed order through shared memory
+    // (the staging ring is idle now).  Layout [rows_per_cta][tpr * K * VEC] fp32.
+    float* fold = reinterpret_cast<float*>(smem_raw);
+    const int width = p.tpr * K * VEC;
+    for (int which = 0; which < (DB ? 2 : 1); ++which) {
+      float* dst = which == 0 ? a.dw_partial : a.db_partial;
+      __syncthreads();
+      if (dst != nullptr) {
+#pragma unroll
+        for (int k = 0; k < K; ++k)
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) {
+            float val = dw[k][i];
+            if constexpr (DB) val = which == 0 ? dw[k][i] : db[k][i];
+            fold[g.r * width + (k * p.tpr + g.t) * VEC + i] = val;
+          }
+      }
+      __syncthreads();
+      if (dst != nullptr) {
+        for (int c = threadIdx.x; c < width; c += nthreads) {
+          if (c < ncols) {
+            float acc = 0.0f;
+            for (int r = 0; r < p.rows_per_cta; ++r) acc += fold[r * width + c];
+            dst[prow + col0 + c] = acc;
+          }
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// stage 2: out[c] = sum_p partial[p, c], fixed order, cast to the parameter dtype
+// ---------------------------------------------------------------------------------------------
+struct ColsumParams {
+  qb_colsum_args a;
+};
+
+// Block (32, 8): 32 consecutive columns x 8 interleaved slices of P.  Each thread adds its
+// partial rows p = ty, ty + 8, ... in increasing order; the 8 slices are then folded in slice
+// order by the ty == 0 threads.  The summation order depends only on P, never on timing.
+__global__ void __launch_bounds__(256) colsum_kernel(const ColsumParams p) {
+  __shared__ float part[8][33];
+  const qb_colsum_args& a = p.a;
+  const int tx = threadIdx.x & 31;
+  const int ty = threadIdx.x >> 5;
+  const int64_t c = static_cast<int64_t>(blockIdx.x) * 32 + tx;
+  float acc = 0.0f;
+  if (c < a.cols) {
+    for (int64_t r = ty; r < a.P; r += 8) acc += a.partial[r * a.cols + c];
+  }
+  part[ty][tx] = acc;
+  __syncthreads();
+  if (ty == 0 && c < a.cols) {
+    float s = part[0][tx];
+#pragma unroll
+    for (int j = 1; j < 8; ++j) s += part[j][tx];
+    if (a.out_f32 != nullptr) a.out_f32[c] = s;
+    if (a.out != nullptr) {
+      if (a.out_dtype == QB_F32) reinterpret_cast<float*>(a.out)[c] = s;
+      else if (a.out_dtype == QB_BF16) reinterpret_cast<__nv_bfloat16*>(a.out)[c] = __float2bfloat16_rn(s);
+      else reinterpret_cast<__half*>(a.out)[c] = __float2half_rn(s);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------------------------
+template <int DT, int VEC, int K>
+static int launch_norm_bwd_k(const NormBwdParams& p, dim3 grid, int threads, size_t smem,
+                             cudaStream_t st) {
+  const bool ln = p.a.is_layernorm != 0;
+  const bool db = p.a.db_partial != nullptr;
+  if constexpr (DT == kDynDT) {
+    // The generic path always carries db accumulators (written only when requested).
+    if (ln) return launch_kernel(norm_bwd_kernel<DT, VEC, K, true, true>, grid, threads, smem,
+                                 p.cluster_n, st, p, "layernorm_bwd");
+    return launch_kernel(norm_bwd_kernel<DT, VEC, K, false, true>, grid, threads, smem,
+                         p.cluster_n, st, p, "rmsnorm_bwd");
+  } else {
+    if (ln && db) return launch_kernel(norm_bwd_kernel<DT, VEC, K, true, true>, grid, threads, smem,
+                                       p.cluster_n, st, p, "layernorm_bwd");
+    if (ln) return launch_kernel(norm_bwd_kernel<DT, VEC, K, true, false>, grid, threads, smem,
+                                 p.cluster_n, st, p, "layernorm_bwd");
+    if (db) return launch_kernel(norm_bwd_kernel<DT, VEC, K, false, true>, grid, threads, smem,
+                                 p.cluster_n, st, p, "rmsnorm_bwd");
+    return launch_kernel(norm_bwd_kernel<DT, VEC, K, false, false>, grid, threads, smem,
+                         p.cluster_n, st, p, "rmsnorm_bwd");
+  }
+}
+
+template <int DT, int VEC>
+static int launch_norm_bwd_v(const NormBwdParams& p, int K, dim3 grid, int threads, size_t smem,
+                             cudaStream_t st) {
+  switch (K) {
+    case 1: return launch_norm_bwd_k<DT, VEC, 1>(p, grid, threads, smem, st);
+    case 2: return launch_norm_bwd_k<DT, VEC, 2>(p, grid, threads, smem, st);
+    case 4: return launch_norm_bwd_k<DT, VEC, 4>(p, grid, threads, smem, st);
+    case 8:
+      if constexpr (DT != kDynDT) return launch_norm_bwd_k<DT, VEC, 8>(p, grid, threads, smem, st);
+  }
+  return set_error(QB_ERR_UNSUPPORTED, "norm_bwd: no kernel for %d chunks of %d per thread", K, VEC);
+}
+
+struct NormBwdPlan {
+  RowPlan rows;
+  bool uniform;
+  int stages;
+  int n_in;
+  size_t smem;
+};
+
+// Shared launch planning of qb_norm_bwd and qb_norm_bwd_num_partials.
+static int plan_norm_bwd(int64_t N, int vec, bool uniform, int x_dtype, bool has_dres_out,
+                         const qb_launch_cfg& cfg, const DeviceFacts* dev, NormBwdPlan* out) {
+  // Registers per thread: weight + dw (+ db) accumulators + two chunks in flight.
+  // (The generic mixed-dtype kernels exist for at most 4 chunks per thread.)
+  const int dyn = 4 * vec;
+  const ElemCaps caps = uniform ? ElemCaps{vec == 8 ? 64 : 32, 16, 8}
+                                : ElemCaps{dyn, dyn < 16 ? dyn : 16, dyn < 8 ? dyn : 8};
+  const int64_t pref = uniform ? (vec == 8 ? 8192 : 4096) : 2048;
+  if (int rc = plan_rows("norm_bwd", N, vec, caps, pref, 2, 256, cfg, &out->rows)) return rc;
+  out->uniform = uniform;
+  out->n_in = has_dres_out ? 3 : 2;
+  const int slot = uniform ? 16 : 4 * vec;
+  const size_t stage_bytes = (size_t)out->n_in * out->rows.K * out->rows.threads * slot;
+  // Ring depth: as deep as shared memory allows (leaving room for a second CTA on the SM when
+  // the stage is small), at most 4 by default.
+  const size_t budget = (size_t)dev->max_smem_optin - 2048;
+  int stages = cfg.stages > 0 ? cfg.stages : 4;
+  if (stages > kMaxStages) stages = kMaxStages;
+  while (stages > 1 && stage_bytes * stages > budget) --stages;
+  if (stage_bytes * stages > budget)
+    return set_error(QB_ERR_UNSUPPORTED, "norm_bwd: one stage of %zu bytes exceeds shared memory",
+                     stage_bytes);
+  out->stages = stages;
+  out->smem = stage_bytes * stages;
+  (void)x_dtype;
+  return QB_OK;
+}
+
+static int default_num_partials(const NormBwdPlan& plan, const DeviceFacts* dev) {
+  // CTAs that fit one SM, by threads and by shared memory.
+  int per_sm = 2048 / plan.rows.threads;
+  const size_t smem_per_sm = 228 * 1024;
+  const int by_smem = static_cast<int>(smem_per_sm / (plan.smem + 2048));
+  if (per_sm > by_smem) per_sm = by_smem;
+  if (per_sm < 1) per_sm = 1;
+  if (per_sm > 2) per_sm = 2;
+  int clusters = dev->sm_count * per_sm / plan.rows.cluster_n;
+  if (clusters < 1) clusters = 1;
+  return clusters;
+}
+
+}  // namespace qb
+
+using namespace qb;
+
+extern "C" int qb_norm_bwd_num_partials(int64_t N, int32_t x_dtype, int32_t is_layernorm,
+                                        int32_t device) {
+  clear_error();
+  (void)is_layernorm;
+  (void)device;
+  if (N <= 0 || !is_float_dtype(x_dtype)) return set_error(QB_ERR_INVALID, "num_partials: bad arguments");
+  const DeviceFacts* dev = current_device_facts();
+  if (dev == nullptr) return QB_ERR_CUDA;
+  VecWidth vw;
+  vw.limit_elems(N);
+  while (vw.vec * host_dtype_bytes(x_dtype) > 16) vw.vec >>= 1;
+  const bool uniform = vw.vec == 16 / host_dtype_bytes(x_dtype);
+  NormBwdPlan plan;
+  qb_launch_cfg cfg = {};
+  if (int rc = plan_norm_bwd(N, vw.vec, uniform, x_dtype, false, cfg, dev, &plan)) return rc;
+  return default_num_partials(plan, dev);
+}
+
+extern "C" int qb_norm_bwd(const qb_norm_bwd_args* args, qb_stream_t stream) {
+  clear_error();
+  if (args == nullptr) return set_error(QB_ERR_INVALID, "norm_bwd: null argument block");
+  const qb_norm_bwd_args& a = *args;
+  if (a.x == nullptr || a.dout == nullptr || a.rstd == nullptr || a.dx == nullptr)
+    return set_error(QB_ERR_INVALID, "norm_bwd: x, dout, rstd and dx are required");
+  if ((a.mean != nullptr) != (a.is_layernorm != 0))
+    return set_error(QB_ERR_INVALID, "norm_bwd: mean is required iff is_layernorm");
+  if (a.M < 0 || a.N <= 0 || a.H <= 0 || a.N > (1 << 30) || a.H > 65535)
+    return set_error(QB_ERR_INVALID, "norm_bwd: bad sizes M=%lld H=%lld N=%lld", (long long)a.M,
+                     (long long)a.H, (long long)a.N);
+  if (!is_float_dtype(a.x_dtype) || !is_float_dtype(a.dout_dtype) || !is_float_dtype(a.dx_dtype) ||
+      (a.weight && !is_float_dtype(a.weight_dtype)) ||
+      (a.dresidual_out && !is_float_dtype(a.dresidual_out_dtype)) ||
+      (a.dresidual && !is_float_dtype(a.dresidual_dtype)))
+    return set_error(QB_ERR_INVALID, "norm_bwd: unsupported dtype code");
+  if ((a.dw_partial != nullptr || a.db_partial != nullptr) && a.num_partials <= 0)
+    return set_error(QB_ERR_INVALID, "norm_bwd: num_partials must be positive");
+  const DeviceFacts* dev = current_device_facts();
+  if (dev == nullptr) return QB_ERR_CUDA;
+
+  VecWidth vw;
+  vw.limit_elems(a.N);
+  vw.add_tensor(a.x, a.x_dtype, a.x_row_stride);
+  vw.add_tensor(a.dout, a.dout_dtype, a.dout_row_stride);
+  vw.add_tensor(a.dx, a.dx_dtype, a.dx_row_stride);
+  vw.add_tensor(a.dresidual_out, a.dresidual_out_dtype, a.dresidual_out_row_stride);
+  vw.add_tensor(a.dresidual, a.dresidual_dtype, a.dresidual_row_stride);
+  vw.add_param(a.weight, a.weight_dtype);
+  vw.add_param(a.dw_partial, QB_F32);
+  vw.add_param(a.db_partial, QB_F32);
+  const int vec = vw.vec;
+  bool uniform = a.dout_dtype == a.x_dtype && a.dx_dtype == a.x_dtype &&
+                 (!a.dresidual_out || a.dresidual_out_dtype == a.x_dtype) &&
+                 (!a.dresidual || a.dresidual_dtype == a.x_dtype);
+  if (vec != 16 / host_dtype_bytes(a.x_dtype)) uniform = false;
+
+  NormBwdPlan plan;
+  if (int rc = plan_norm_bwd(a.N, vec, uniform, a.x_dtype, a.dresidual_out != nullptr, a.cfg, dev,
+                             &plan))
+    return rc;
+
+  NormBwdParams p;
+  p.a = a;
+  p.tpr = plan.rows.tpr;
+  p.rows_per_cta = plan.rows.rows_per_cta;
+  p.cluster_n = plan.rows.cluster_n;
+  p.cols_per_cta = plan.rows.cols_per_cta;
+  p.num_tiles = ceil_div(a.M, p.rows_per_cta);
+  p.stages = plan.stages;
+  p.n_in = plan.n_in;
+  // The grid is fixed by the workspace: one CTA (cluster) per partial-sum slice.
+  int64_t clusters = (a.dw_partial != nullptr || a.db_partial != nullptr)
+                         ? a.num_partials
+                         : (a.cfg.max_ctas > 0 ? a.cfg.max_ctas / plan.rows.cluster_n
+                                               : default_num_partials(plan, dev));
+  if (clusters < 1) clusters = 1;
+  if (clusters * plan.rows.cluster_n > 0x7fffffffLL)
+    return set_error(QB_ERR_INVALID, "norm_bwd: num_partials too large");
+  dim3 grid(static_cast<unsigned>(clusters * plan.rows.cluster_n), static_cast<unsigned>(a.H), 1);
+  // The fold of multi-row CTAs reuses the ring: make sure it is large enough.
+  size_t smem = plan.smem;
+  const size_t fold_bytes =
+      p.rows_per_cta > 1 ? (size_t)plan.rows.threads * plan.rows.K * vec * 4 : 0;
+  if (smem < fold_bytes) smem = fold_bytes;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+
+  if (uniform) {
+    switch (a.x_dtype) {
+      case QB_BF16: return launch_norm_bwd_v<QB_BF16, 8>(p, plan.rows.K, grid, plan.rows.threads, smem, st);
+      case QB_F16: return launch_norm_bwd_v<QB_F16, 8>(p, plan.rows.K, grid, plan.rows.threads, smem, st);
+      default: return launch_norm_bwd_v<QB_F32, 4>(p, plan.rows.K, grid, plan.rows.threads, smem, st);
+    }
+  }
+  switch (vec) {
+    case 8: return launch_norm_bwd_v<kDynDT, 8>(p, plan.rows.K, grid, plan.rows.threads, smem, st);
+    case 4: return launch_norm_bwd_v<kDynDT, 4>(p, plan.rows.K, grid, plan.rows.threads, smem, st);
+    case 2: return launch_norm_bwd_v<kDynDT, 2>(p, plan.rows.K, grid, plan.rows.threads, smem, st);
+    default: return launch_norm_bwd_v<kDynDT, 1>(p, plan.rows.K, grid, plan.rows.threads, smem, st);
+  }
+}
+
+extern "C" int qb_colsum(const qb_colsum_args* args, qb_stream_t stream) {
+  clear_error();
+  if (args == nullptr) return set_error(QB_ERR_INVALID, "colsum: null argument block");
+  const qb_colsum_args& a = *args;
+  if (a.partial == nullptr || (a.out == nullptr && a.out_f32 == nullptr))
+    return set_error(QB_ERR_INVALID, "colsum: partial and an output are required");
+  if (a.P < 0 || a.cols < 0) return set_error(QB_ERR_INVALID, "colsum: bad sizes");
+  if (a.out != nullptr && !is_float_dtype(a.out_dtype))
+    return set_error(QB_ERR_INVALID, "colsum: unsupported dtype code");
+  if (a.cols == 0) return QB_OK;
+  ColsumParams p;
+  p.a = a;
+  dim3 grid(static_cast<unsigned>(ceil_div(a.cols, 32)), 1, 1);
+  return launch_kernel(colsum_kernel, grid, 256, 0, 1, reinterpret_cast<cudaStream_t>(stream), p,
+                       "colsum");
+}

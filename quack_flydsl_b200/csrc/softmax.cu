@@ -1,0 +1,291 @@
+// Softmax forward and backward over the last dimension, for sm_100a.
+//
+// Forward follows quack/softmax.py:87-176 (Softmax.kernel, online (max, sum-exp) pair combined in
+// one exchange, quack/reduce.py:227-324); backward follows quack/softmax.py:275-353
+// (SoftmaxBackward.kernel).  A row is read once, kept in registers, and written once; rows longer
+// than one CTA's register capacity are split over a thread-block cluster whose CTAs exchange
+// their partials through distributed shared memory.
+#include "common.cuh"
+#include "host_common.h"
+
+namespace qb {
+
+struct SoftmaxParams {
+  const void* in0;  // fwd: x        bwd: dy
+  const void* in1;  // fwd: unused   bwd: y
+  void* out;        // fwd: y        bwd: dx
+  int64_t M;
+  int N;
+  int64_t ld0, ld1, ldo;
+  int dt0, dt1, dto;
+  int tpr, rows_per_cta, cluster_n, cols_per_cta;
+  int64_t num_tiles;
+};
+
+template <int DT, int VEC, int K>
+__global__ void __launch_bounds__((K * VEC > 16) ? 512 : 1024)
+softmax_fwd_kernel(const SoftmaxParams p) {
+  __shared__ ReduceScratch scratch;
+  const RowGeom g = make_geom(p.tpr, p.cluster_n);
+  if (p.cluster_n > 1) cluster_arrive();
+  const int col0 = static_cast<int>(g.crank) * p.cols_per_cta;
+  const int ncols = min(p.cols_per_cta, p.N - col0);
+  int col[K];
+  bool cok[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const int local = (k * p.tpr + g.t) * VEC;
+    cok[k] = local < ncols;
+    col[k] = col0 + local;
+  }
+  const int64_t tile_stride = gridDim.x / p.cluster_n;
+  int parity = 0;
+  bool first = true;
+  for (int64_t tile = blockIdx.x / p.cluster_n; tile < p.num_tiles; tile += tile_stride) {
+    const int64_t row = tile * p.rows_per_cta + g.r;
+    const bool row_ok = row < p.M;
+    float v[K][VEC];
+    {
+      uint32_t rx[K][RawWords<DT, VEC>::value];
+#pragma unroll
+      for (int k = 0; k < K; ++k)
+        load_chunk_raw<DT, VEC>(rx[k], p.in0, row * p.ld0 + col[k], p.dt0, row_ok && cok[k]);
+#pragma unroll
+      for (int k = 0; k < K; ++k) unpack_chunk<DT, VEC>(v[k], rx[k], p.dt0);
+    }
+    // Thread-local maximum over the lanes that exist.
+    float m_t = neg_inf();
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      if (row_ok && cok[k]) {
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) m_t = fmaxf(m_t, v[k][i]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) v[k][i] = neg_inf();
+      }
+    }
+    // e_i = exp(x_i - m_t) as exp2 of one fused multiply-add; one exponential per element.
+    const float nm = (m_t == neg_inf()) ? 0.0f : -m_t * kLog2e;
+    float s_t = 0.0f;
+#pragma unroll
+    for (int k = 0; k < K; ++k)
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) {
+        v[k][i] = fast_exp2(fmaf(v[k][i], kLog2e, nm));
+        s_t += v[k][i];
+      }
+    if (first && p.cluster_n > 1) cluster_wait();
+    first = false;
+    const float2 ms = row_reduce<MaxSumExpOp>(make_float2(m_t, s_t), g, scratch, 0, parity);
+    parity ^= 1;
+    // y_i = e_i * exp(m_t - m) / s
+    const float scale =
+        (m_t == neg_inf()) ? 0.0f : fast_exp2((m_t - ms.x) * kLog2e) * (1.0f / ms.y);
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      float y[VEC];
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) y[i] = v[k][i] * scale;
+      if (row_ok && cok[k]) store_chunk<DT, VEC>(p.out, row * p.ldo + col[k], y, p.dto);
+    }
+  }
+  if (first && p.cluster_n > 1) cluster_wait();
+}
+
+// dx = y * (dy - sum(dy * y)).  dy and y stay packed in registers; they are unpacked once for the
+// dot product and once more for the output.
+template <int DT, int VEC, int K>
+__global__ void __launch_bounds__((K * VEC > 16) ? 512 : 1024)
+softmax_bwd_kernel(const SoftmaxParams p) {
+  __shared__ ReduceScratch scratch;
+  const RowGeom g = make_geom(p.tpr, p.cluster_n);
+  if (p.cluster_n > 1) cluster_arrive();
+  const int col0 = static_cast<int>(g.crank) * p.cols_per_cta;
+  const int ncols = min(p.cols_per_cta, p.N - col0);
+  int col[K];
+  bool cok[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const int local = (k * p.tpr + g.t) * VEC;
+    cok[k] = local < ncols;
+    col[k] = col0 + local;
+  }
+  const int64_t tile_stride = gridDim.x / p.cluster_n;
+  int parity = 0;
+  bool first = true;
+  for (int64_t tile = blockIdx.x / p.cluster_n; tile < p.num_tiles; tile += tile_stride) {
+    const int64_t row = tile * p.rows_per_cta + g.r;
+    const bool row_ok = row < p.M;
+    uint32_t rdy[K][RawWords<DT, VEC>::value];
+    uint32_t ry[K][RawWords<DT, VEC>::value];
+#pragma unroll
+    for (int k = 0; k < K; ++k)
+      load_chunk_raw<DT, VEC>(rdy[k], p.in0, row * p.ld0 + col[k], p.dt0, row_ok && cok[k]);
+#pragma unroll
+    for (int k = 0; k < K; ++k)
+      load_chunk_raw<DT, VEC>(ry[k], p.in1, row * p.ld1 + col[k], p.dt1, row_ok && cok[k]);
+    float dot = 0.0f;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      float dy[VEC], y[VEC];
+      unpack_chunk<DT, VEC>(dy, rdy[k], p.dt0);
+      unpack_chunk<DT, VEC>(y, ry[k], p.dt1);
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) dot = fmaf(dy[i], y[i], dot);
+    }
+    if (first && p.cluster_n > 1) cluster_wait();
+    first = false;
+    dot = row_reduce<SumOp>(make_float2(dot, 0.f), g, scratch, 0, parity).x;
+    parity ^= 1;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      float dy[VEC], y[VEC], dx[VEC];
+      unpack_chunk<DT, VEC>(dy, rdy[k], p.dt0);
+      unpack_chunk<DT, VEC>(y, ry[k], p.dt1);
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) dx[i] = y[i] * (dy[i] - dot);
+      if (row_ok && cok[k]) store_chunk<DT, VEC>(p.out, row * p.ldo + col[k], dx, p.dto);
+    }
+  }
+  if (first && p.cluster_n > 1) cluster_wait();
+}
+
+// ---------------------------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------------------------
+template <int DT, int VEC, bool BWD>
+static int launch_softmax_v(const SoftmaxParams& p, int K, dim3 grid, int threads,
+                            cudaStream_t st) {
+  const char* name = BWD ? "softmax_bwd" : "softmax_fwd";
+#define QB_CASE(KK)                                                                             \
+  case KK:                                                                                      \
+    if constexpr (BWD)                                                                          \
+      return launch_kernel(softmax_bwd_kernel<DT, VEC, KK>, grid, threads, 0, p.cluster_n, st,  \
+                           p, name);                                                            \
+    else                                                                                        \
+      return launch_kernel(softmax_fwd_kernel<DT, VEC, KK>, grid, threads, 0, p.cluster_n, st,  \
+                           p, name);
+  switch (K) {
+    QB_CASE(1)
+    QB_CASE(2)
+    QB_CASE(4)
+    QB_CASE(8)
+    case 16:
+      if constexpr (VEC <= 4) {
+        if constexpr (BWD)
+          return launch_kernel(softmax_bwd_kernel<DT, VEC, 16>, grid, threads, 0, p.cluster_n, st,
+                               p, name);
+        else
+          return launch_kernel(softmax_fwd_kernel<DT, VEC, 16>, grid, threads, 0, p.cluster_n, st,
+                               p, name);
+      }
+  }
+#undef QB_CASE
+  return set_error(QB_ERR_UNSUPPORTED, "%s: no kernel for %d chunks of %d per thread", name, K, VEC);
+}
+
+template <bool BWD>
+static int softmax_dispatch(SoftmaxParams& p, bool uniform, int vec, const qb_launch_cfg& cfg,
+                            cudaStream_t st) {
+  const DeviceFacts* dev = current_device_facts();
+  if (dev == nullptr) return QB_ERR_CUDA;
+  RowPlan plan;
+  // fwd holds the row as fp32 (64 per thread up to 512 threads); bwd holds two packed tensors.
+  const ElemCaps caps = {uniform ? 64 : 32, uniform ? 64 : 32, 16};
+  const int64_t pref = (uniform && vec == 8) ? 16384 : 8192;
+  if (int rc = plan_rows(BWD ? "softmax_bwd" : "softmax_fwd", p.N, vec, caps, pref, 4, 256, cfg,
+                         &plan))
+    return rc;
+  p.tpr = plan.tpr;
+  p.rows_per_cta = plan.rows_per_cta;
+  p.cluster_n = plan.cluster_n;
+  p.cols_per_cta = plan.cols_per_cta;
+  p.num_tiles = ceil_div(p.M, p.rows_per_cta);
+  const int64_t max_ctas =
+      cfg.max_ctas > 0 ? cfg.max_ctas : (int64_t)dev->sm_count * (2048 / plan.threads) * 2;
+  int64_t clusters = p.num_tiles;
+  if (clusters > max_ctas / plan.cluster_n) clusters = max_ctas / plan.cluster_n;
+  if (clusters < 1) clusters = 1;
+  dim3 grid(static_cast<unsigned>(clusters * plan.cluster_n), 1, 1);
+  if (uniform) {
+    switch (p.dt0) {
+      case QB_BF16: return launch_softmax_v<QB_BF16, 8, BWD>(p, plan.K, grid, plan.threads, st);
+      case QB_F16: return launch_softmax_v<QB_F16, 8, BWD>(p, plan.K, grid, plan.threads, st);
+      default: return launch_softmax_v<QB_F32, 4, BWD>(p, plan.K, grid, plan.threads, st);
+    }
+  }
+  switch (vec) {
+    case 8: return launch_softmax_v<kDynDT, 8, BWD>(p, plan.K, grid, plan.threads, st);
+    case 4: return launch_softmax_v<kDynDT, 4, BWD>(p, plan.K, grid, plan.threads, st);
+    case 2: return launch_softmax_v<kDynDT, 2, BWD>(p, plan.K, grid, plan.threads, st);
+    default: return launch_softmax_v<kDynDT, 1, BWD>(p, plan.K, grid, plan.threads, st);
+  }
+}
+
+}  // namespace qb
+
+using namespace qb;
+
+extern "C" int qb_softmax_fwd(const qb_softmax_fwd_args* args, qb_stream_t stream) {
+  clear_error();
+  if (args == nullptr) return set_error(QB_ERR_INVALID, "softmax_fwd: null argument block");
+  const qb_softmax_fwd_args& a = *args;
+  if (a.x == nullptr || a.out == nullptr)
+    return set_error(QB_ERR_INVALID, "softmax_fwd: x and out are required");
+  if (a.M < 0 || a.N <= 0 || a.N > (1 << 30))
+    return set_error(QB_ERR_INVALID, "softmax_fwd: bad sizes M=%lld N=%lld", (long long)a.M,
+                     (long long)a.N);
+  if (!is_float_dtype(a.x_dtype) || !is_float_dtype(a.out_dtype))
+    return set_error(QB_ERR_INVALID, "softmax_fwd: unsupported dtype code");
+  if (a.M == 0) return QB_OK;
+  VecWidth vw;
+  vw.limit_elems(a.N);
+  vw.add_tensor(a.x, a.x_dtype, a.x_row_stride);
+  vw.add_tensor(a.out, a.out_dtype, a.out_row_stride);
+  const bool uniform = a.x_dtype == a.out_dtype && vw.vec == 16 / host_dtype_bytes(a.x_dtype);
+  SoftmaxParams p = {};
+  p.in0 = a.x;
+  p.out = a.out;
+  p.M = a.M;
+  p.N = static_cast<int>(a.N);
+  p.ld0 = a.x_row_stride;
+  p.ldo = a.out_row_stride;
+  p.dt0 = a.x_dtype;
+  p.dto = a.out_dtype;
+  return softmax_dispatch<false>(p, uniform, vw.vec, a.cfg, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int qb_softmax_bwd(const qb_softmax_bwd_args* args, qb_stream_t stream) {
+  clear_error();
+  if (args == nullptr) return set_error(QB_ERR_INVALID, "softmax_bwd: null argument block");
+  const qb_softmax_bwd_args& a = *args;
+  if (a.dy == nullptr || a.y == nullptr || a.dx == nullptr)
+    return set_error(QB_ERR_INVALID, "softmax_bwd: dy, y and dx are required");
+  if (a.M < 0 || a.N <= 0 || a.N > (1 << 30))
+    return set_error(QB_ERR_INVALID, "softmax_bwd: bad sizes M=%lld N=%lld", (long long)a.M,
+                     (long long)a.N);
+  if (!is_float_dtype(a.dy_dtype) || !is_float_dtype(a.y_dtype) || !is_float_dtype(a.dx_dtype))
+    return set_error(QB_ERR_INVALID, "softmax_bwd: unsupported dtype code");
+  if (a.M == 0) return QB_OK;
+  VecWidth vw;
+  vw.limit_elems(a.N);
+  vw.add_tensor(a.dy, a.dy_dtype, a.dy_row_stride);
+  vw.add_tensor(a.y, a.y_dtype, a.y_row_stride);
+  vw.add_tensor(a.dx, a.dx_dtype, a.dx_row_stride);
+  const bool uniform = a.dy_dtype == a.y_dtype && a.dy_dtype == a.dx_dtype &&
+                       vw.vec == 16 / host_dtype_bytes(a.dy_dtype);
+  SoftmaxParams p = {};
+  p.in0 = a.dy;
+  p.in1 = a.y;
+  p.out = a.dx;
+  p.M = a.M;
+  p.N = static_cast<int>(a.N);
+  p.ld0 = a.dy_row_stride;
+  p.ld1 = a.y_row_stride;
+  p.ldo = a.dx_row_stride;
+  p.dt0 = a.dy_dtype;
+  p.dt1 = a.y_dtype;
+  p.dto = a.dx_dtype;
+  return softmax_dispatch<true>(p, uniform, vw.vec, a.cfg, reinterpret_cast<cudaStream_t>(stream));
+}

@@ -1,0 +1,148 @@
+"""Launch configuration of the RMSNorm / LayerNorm kernels (sm_100a only).
+
+Mirrors the public surface of the reference's quack/rmsnorm_config.py:16-26,94-107,265-293:
+the two frozen dataclasses, their ``from_analytical_heuristic`` factories, ``get_sm_count`` and
+the explicit-config search spaces used by the tuned entry points.  The knobs that describe the
+reference's shared-memory reload strategy (``reload_from``, ``delay_w_load``, ``reload_wdy``,
+``reload_x``, ``use_tma``) are accepted for signature compatibility and ignored: the sm_100a
+kernels keep rows in registers (forward) or in a cp.async ring (backward).
+"""
+
+from __future__ import annotations
+
+import itertools
+from dataclasses import dataclass
+from typing import List, Optional
+
+import torch
+
+
+@dataclass(frozen=True)
+class RmsNormFwdConfig:
+    num_threads: int
+    threads_per_row: int
+    cluster_n: int
+    reload_from: Optional[str] = None
+    delay_w_load: bool = False
+
+    @classmethod
+    def from_analytical_heuristic(cls, N: int, dtype_width: int, arch_major: Optional[int] = None,
+                                  is_layernorm: bool = False) -> "RmsNormFwdConfig":
+        """The configuration the C launcher's heuristic picks for an aligned row of N elements."""
+        vec = 128 // dtype_width
+        threads, tpr, cluster_n = _plan(N, vec, pref_elems=16384 if vec == 8 else 8192,
+                                        k_target=4, caps=(64, 64, 16))
+        return cls(num_threads=threads, threads_per_row=tpr, cluster_n=cluster_n)
+
+
+@dataclass(frozen=True)
+class RmsNormBwdConfig:
+    num_threads: int
+    threads_per_row: int
+    cluster_n: int
+    reload_wdy: Optional[str] = None
+    reload_x: Optional[str] = None
+    use_tma: bool = False
+    smem_stages: int = 0  # cp.async ring depth; 0 = as deep as shared memory allows (<= 4)
+
+    @classmethod
+    def from_analytical_heuristic(cls, N: int, dtype_width: int, dout_width: Optional[int] = None,
+                                  arch_major: Optional[int] = None, T_hint: int = 0,
+                                  num_acc: int = 1) -> "RmsNormBwdConfig":
+        vec = 128 // max(dtype_width, dout_width or dtype_width)
+        threads, tpr, cluster_n = _plan(N, vec, pref_elems=8192 if vec == 8 else 4096,
+                                        k_target=2, caps=(64 if vec == 8 else 32, 16, 8))
+        return cls(num_threads=threads, threads_per_row=tpr, cluster_n=cluster_n)
+
+
+def _next_pow2(v: int) -> int:
+    return 1 << max(0, (int(v) - 1).bit_length())
+
+
+def _max_k(caps, threads: int, vec: int) -> int:
+    cap = caps[2] if threads > 512 else (caps[1] if threads > 256 else caps[0])
+    kmax = 16 if vec <= 4 else 8
+    k = 1
+    while k * 2 <= kmax and k * 2 * vec <= cap:
+        k *= 2
+    return k if k * vec <= cap else 0
+
+
+def _plan(N: int, vec: int, pref_elems: int, k_target: int, caps, default_threads: int = 256):
+    """Python restatement of the C launcher's geometry search (csrc/host_common.h: plan_rows)
+    for the no-override case; used for reporting and for sizing the backward workspace."""
+    while vec > 1 and N % vec:
+        vec //= 2
+    chunks = N // vec
+    max_cap = max(t * _max_k(caps, t, vec) for t in (32, 64, 128, 256, 512, 1024))
+    cluster_n = 1
+    pref = min(pref_elems // vec, max_cap)
+    while -(-chunks // cluster_n) > pref and cluster_n < 8:
+        cluster_n *= 2
+    if -(-chunks // cluster_n) > max_cap:
+        cluster_n = 16
+    while cluster_n > 1 and (cluster_n - 1) * -(-chunks // cluster_n) >= chunks:
+        cluster_n //= 2
+    cpc = -(-chunks // cluster_n)
+    lo = 32 if cluster_n > 1 else 8
+    want = min(1024, max(lo, _next_pow2(-(-cpc // k_target))))
+    order = []
+    t = want
+    while t <= 1024:
+        order.append(t)
+        t *= 2
+    t = want // 2
+    while t >= lo:
+        order.append(t)
+        t //= 2
+    tpr = 0
+    for t in order:
+        if -(-cpc // t) <= _max_k(caps, max(t, 32), vec):
+            tpr = t
+            break
+    if tpr == 0:
+        raise ValueError(f"a row of {N} elements does not fit (vector width {vec})")
+    if cluster_n > 1:
+        tpr = max(tpr, 32)
+        return tpr, tpr, cluster_n
+    K = _next_pow2(-(-cpc // tpr))
+    threads = max(tpr, 32)
+    while threads < default_threads and K <= _max_k(caps, threads * 2, vec):
+        threads *= 2
+    return threads, tpr, cluster_n
+
+
+def get_sm_count(N: int, device, dtype: Optional[torch.dtype] = None) -> int:
+    """Number of partial-sum slices (persistent CTAs or clusters) the backward kernel uses by
+    default, i.e. the first dimension of ``dw_partial`` (reference: quack/rmsnorm_config.py:265-293).
+
+    Pure Python on purpose: it runs inside ``torch.compile`` traces.  Any positive value is
+    functionally valid; this one gives one persistent CTA (or two, for short rows whose ring
+    leaves room) per SM, divided by the cluster size for rows split over a cluster."""
+    props = torch.cuda.get_device_properties(device)
+    sms = props.multi_processor_count
+    width = 32 if dtype == torch.float32 else 16
+    cfg = RmsNormBwdConfig.from_analytical_heuristic(N, width)
+    per_sm = 2 if cfg.num_threads <= 512 and N * (width // 8) <= 8192 else 1
+    return max(1, (sms * per_sm) // cfg.cluster_n)
+
+
+_CTA_THREAD_SIZE = (128, 256, 512)
+_THREADS_PER_ROW = (32, 64, 128, 256, 512)
+_CLUSTER_N = (1, 2, 4, 8)
+
+
+def get_all_fwd_configs() -> List[RmsNormFwdConfig]:
+    out = []
+    for nt, tpr, cn in itertools.product(_CTA_THREAD_SIZE, _THREADS_PER_ROW, _CLUSTER_N):
+        if tpr <= nt:
+            out.append(RmsNormFwdConfig(nt, tpr, cn))
+    return out
+
+
+def get_all_bwd_configs() -> List[RmsNormBwdConfig]:
+    out = []
+    for nt, tpr, cn, st in itertools.product(_CTA_THREAD_SIZE, _THREADS_PER_ROW, _CLUSTER_N, (2, 3, 4)):
+        if tpr <= nt:
+            out.append(RmsNormBwdConfig(nt, tpr, cn, smem_stages=st))
+    return out
