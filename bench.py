@@ -1,0 +1,479 @@
+"""Benchmark of the row-reduction hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-suite]
+
+A step is one pass of the headline workload -- RMSNorm forward + backward, bf16 [32768, 8192] with
+a residual (weight bf16, eps 1e-6) -- on every rank (weak scaling: each GPU owns its own 32768
+rows; ranks exchange only the dw all-reduce).  The reported value is the reference's "model
+memory throughput": algorithmic bytes of forward + backward (benchmarks/benchmark_rmsnorm.py:107-111,
+219-229) divided by the step time, summed over ranks.  Rank 0 prints ONE JSON line.
+
+``--impl reference`` times the reference's own CPU path (its PyTorch reference functions, restated
+in oracle/) on the host cores, on a bounded row sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+M_ROWS, N_COLS = 32768, 8192
+EPS = 1e-6
+METRIC = "RMSNorm/LN/softmax/CE fwd+bwd HBM GB/s"
+WORKLOAD = "RMSNorm fwd+bwd bf16 [32768,8192] + residual (weight bf16, eps 1e-6), per GPU"
+NOMINAL_HBM_GBS = 8000.0
+FALLBACK_PEAK_GBS = 6650.0
+
+
+def fwd_bytes(M, N, s=2):
+    # x, residual in; out, residual_out back; weight; rstd
+    return 4 * M * N * s + N * s + M * 4
+
+
+def bwd_bytes(M, N, s=2):
+    # x, dout in; dx out; weight in; rstd in; dw out
+    return 3 * M * N * s + N * s + M * 4 + N * s
+
+
+def measured_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+        except Exception:
+            pass
+    return FALLBACK_PEAK_GBS, "fallback (6.65 TB/s)"
+
+
+# ------------------------------------------------------------------------------------------------
+# clocks
+# ------------------------------------------------------------------------------------------------
+class ClockSampler:
+    """Samples SM clocks and throttle reasons with nvidia-smi while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.gpu)],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, smax, reasons, power = [], [], set(), []
+        try:
+            for line in open(self.path):
+                f = [c.strip() for c in line.split(",")]
+                if len(f) < 9:
+                    continue
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+                try:
+                    power.append(float(f[3]))
+                except ValueError:
+                    pass
+                for name, val in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown",
+                                      "sw_power_cap"), f[5:9]):
+                    if val.lower().startswith("active"):
+                        reasons.add(name)
+            os.unlink(self.path)
+        except Exception:
+            pass
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm), "power_w_max": max(power) if power else None}
+
+
+# ------------------------------------------------------------------------------------------------
+# CPU arm (reference's PyTorch CPU path, restated in oracle/)
+# ------------------------------------------------------------------------------------------------
+def cpu_step(d):
+    import oracle
+
+    out, h = oracle.rmsnorm_ref(d["x"], d["weight"], residual=d["residual"], eps=EPS)
+    rstd = oracle.rmsnorm_rstd_ref(h, eps=EPS)
+    dx, dw, _ = oracle.rmsnorm_bwd_ref(h, d["weight"], d["dout"], rstd)
+    return out, h, rstd, dx.to(torch.bfloat16), dw.to(torch.bfloat16)
+
+
+def cpu_baseline(rows: int, repeats: int = 3, warmup: int = 1) -> dict:
+    import oracle
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    d = oracle.make_config_inputs("c2", rows=rows)
+    for _ in range(warmup):
+        cpu_step(d)
+    best = float("inf")
+    for _ in range(repeats):
+        t0 = time.perf_counter()
+        cpu_step(d)
+        best = min(best, time.perf_counter() - t0)
+    nbytes = fwd_bytes(rows, N_COLS) + bwd_bytes(rows, N_COLS)
+    return {"value": nbytes / best / 1e9, "unit": "GB/s", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"first {rows} of {M_ROWS} rows of the workload (full N={N_COLS}), best of {repeats}, "
+                      f"{best * 1e3:.1f} ms per fwd+bwd pass",
+            "ms": best * 1e3}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import oracle
+
+    rows = 2048
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    d = oracle.make_config_inputs("c2", rows=rows)
+    for _ in range(max(args.warmup, 1)):
+        cpu_step(d)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_step(d)
+    dt = (time.perf_counter() - t0) / args.steps
+    nbytes = fwd_bytes(rows, N_COLS) + bwd_bytes(rows, N_COLS)
+    val = nbytes / dt / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": val, "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": WORKLOAD, "arm": "reference's PyTorch CPU reference functions "
+                   "(rmsnorm_ref / rmsnorm_bwd_ref restated in oracle/), host cores only",
+                   "sample_rows": rows},
+        "cpu_baseline": {"value": val, "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": f"each step = first {rows} of {M_ROWS} rows, full N={N_COLS}"},
+        "e2e": {"value": val, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------------------
+# GPU arm
+# ------------------------------------------------------------------------------------------------
+class Timeline:
+    """CUDA-event pairs around individual launches on the current stream."""
+
+    def __init__(self):
+        self.spans = {}
+
+    def run(self, name, fn):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        self.spans.setdefault(name, []).append((a, b))
+
+    def mean_ms(self):
+        return {k: sum(a.elapsed_time(b) for a, b in v) / len(v) for k, v in self.spans.items()}
+
+    def count(self):
+        return sum(len(v) for v in self.spans.values())
+
+
+def time_kernel(fn, iters=10, warmup=3):
+    """Mean device time of fn() in ms: one CUDA-event pair per launch (inputs exceed L2)."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    pairs = []
+    for _ in range(iters):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        pairs.append((a, b))
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in pairs) / len(pairs)
+
+
+def suite(dev, peak) -> dict:
+    """Every other kernel of the hot path at its BASELINE configuration: mean device ms, GB/s of
+    algorithmic bytes and the fraction of the measured copy peak.  Outside the timed region."""
+    import importlib
+
+    rn = importlib.import_module("quack_flydsl_b200.rmsnorm")
+    sm = importlib.import_module("quack_flydsl_b200.softmax")
+    ce = importlib.import_module("quack_flydsl_b200.cross_entropy")
+    from quack_flydsl_b200.rmsnorm_config import get_sm_count
+
+    res = {}
+
+    def rec(name, ms, nbytes):
+        gbs = nbytes / ms / 1e6
+        res[name] = {"ms": round(ms, 4), "gbs": round(gbs, 1), "frac_of_measured_peak": round(gbs / peak, 4),
+                     "pct_of_8TBs": round(100 * gbs / NOMINAL_HBM_GBS, 2), "bytes": nbytes}
+
+    g = torch.Generator(device=dev).manual_seed(1)
+    bf = torch.bfloat16
+    # C3 LayerNorm bf16 [65536, 4096]
+    M, N = 65536, 4096
+    x = (0.5 + torch.randn(M, N, device=dev, generator=g)).to(bf)
+    w = (1 + 0.1 * torch.randn(N, device=dev, generator=g)).to(bf)
+    b = (0.1 * torch.randn(N, device=dev, generator=g)).to(bf)
+    dout = torch.randn(M, N, device=dev, generator=g).to(bf)
+    out, dx = torch.empty_like(x), torch.empty_like(x)
+    rstd, mean = torch.empty(M, device=dev), torch.empty(M, device=dev)
+    P = get_sm_count(N, dev, bf)
+    dwp, dbp = torch.empty(P, N, device=dev), torch.empty(P, N, device=dev)
+    dw, db = torch.empty(N, device=dev, dtype=bf), torch.empty(N, device=dev, dtype=bf)
+    rec("layernorm_fwd", time_kernel(lambda: rn._rmsnorm_fwd(x, w, out, b, rstd, mean, None, None, 1e-5, True)),
+        2 * M * N * 2 + 2 * N * 2 + 2 * M * 4)
+    rec("layernorm_bwd", time_kernel(lambda: rn._rmsnorm_bwd(x, w, dout, rstd, dx, dwp, dbp, None, None, P, mean, True)),
+        3 * M * N * 2 + 2 * M * 4 + N * 2 + 2 * N * 2)
+
+    def ln_bwd_total():
+        rn._rmsnorm_bwd(x, w, dout, rstd, dx, dwp, dbp, None, None, P, mean, True)
+        rn._norm_bwd_colsum(dwp, dw)
+        rn._norm_bwd_colsum(dbp, db)
+    rec("layernorm_bwd_with_stage2", time_kernel(ln_bwd_total), 3 * M * N * 2 + 2 * M * 4 + N * 2 + 2 * N * 2)
+    del x, dout, out, dx
+    # C4 softmax bf16, M * N = 2^31
+    for N in (4096, 16384, 65536, 131072):
+        M = (1 << 31) // N
+        x = (3 * torch.randn(M, N, device=dev, generator=g)).to(bf)
+        y = torch.empty_like(x)
+        rec(f"softmax_fwd_N{N}", time_kernel(lambda: sm._softmax_fwd(x, y), iters=5, warmup=2), 2 * M * N * 2)
+        dy = torch.randn(M, N, device=dev, generator=g).to(bf)
+        rec(f"softmax_bwd_N{N}", time_kernel(lambda: sm._softmax_backward(dy, y, x), iters=5, warmup=2), 3 * M * N * 2)
+        del x, y, dy
+    # C5 cross-entropy bf16 [16384, 128256], int64 targets, 5 % ignored
+    M, N = 16384, 128256
+    x = (2 * torch.randn(M, N, device=dev, generator=g)).to(bf)
+    t = torch.randint(0, N, (M,), device=dev, generator=g)
+    t[torch.rand(M, device=dev, generator=g) < 0.05] = -100
+    loss, lse = torch.empty(M, device=dev), torch.empty(M, device=dev)
+    dxl = torch.empty_like(x)
+    dloss = torch.full((M,), 1.0 / M, device=dev)
+    rec("ce_fwd", time_kernel(lambda: ce.cross_entropy_fwd_out(x, t, None, loss, lse, None, None, -100), iters=5, warmup=2),
+        M * N * 2 + 16 * M)
+    rec("ce_bwd", time_kernel(lambda: ce.cross_entropy_bwd_out(x, t, dloss, lse, dxl, None, -100), iters=5, warmup=2),
+        2 * M * N * 2 + 16 * M)
+    return res
+
+
+def run_ours(args) -> None:
+    import importlib
+
+    import torch.distributed as dist
+
+    rn = importlib.import_module("quack_flydsl_b200.rmsnorm")
+    from quack_flydsl_b200 import _C, sharded
+    from quack_flydsl_b200.rmsnorm_config import get_sm_count
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if not torch.cuda.is_available():
+        raise RuntimeError("bench.py needs a CUDA device; there is no CPU path (use --impl reference "
+                           "for the CPU arm)")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    _C.lib()
+    peak, peak_src = measured_peak()
+
+    M, N = M_ROWS, N_COLS
+    bf = torch.bfloat16
+    g = torch.Generator(device=dev).manual_seed(rank)
+    x = torch.randn(M, N, device=dev, generator=g).to(bf)
+    res = torch.randn(M, N, device=dev, generator=g).to(bf)
+    w = (1 + 0.1 * torch.randn(N, device=dev, generator=g)).to(bf)
+    dout = torch.randn(M, N, device=dev, generator=g).to(bf)
+    out, res_out, dx = torch.empty_like(x), torch.empty_like(x), torch.empty_like(x)
+    rstd = torch.empty(M, device=dev)
+    P = get_sm_count(N, dev, bf)
+    dw_partial = torch.empty(P, N, device=dev)
+    dw32 = torch.empty(N, device=dev)
+    dw = torch.empty(N, device=dev, dtype=bf)
+    tl = Timeline()
+
+    def step(record: bool):
+        run = tl.run if record else (lambda _n, f: f())
+        run("rmsnorm_fwd", lambda: rn._rmsnorm_fwd(x, w, out, None, rstd, None, res, res_out, EPS))
+        run("rmsnorm_bwd", lambda: rn._rmsnorm_bwd(res_out, w, dout, rstd, dx, dw_partial, None, None, None, P))
+        if world > 1:
+            run("dw_colsum", lambda: rn._norm_bwd_colsum(dw_partial, dw32))
+            run("dw_allreduce", lambda: sharded.allreduce_param_grads(dw32, None)[0])
+            dw.copy_(dw32)
+        else:
+            run("dw_colsum", lambda: rn._norm_bwd_colsum(dw_partial, dw))
+
+    def sync_all():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+            torch.cuda.synchronize()
+
+    for _ in range(max(args.warmup, 3)):
+        step(False)
+    sync_all()
+    sampler = ClockSampler(local)
+    if rank == 0:
+        sampler.start()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sync_all()
+    t0.record()
+    for _ in range(args.steps):
+        step(True)
+    t1.record()
+    sync_all()
+    clocks = sampler.stop() if rank == 0 else None
+    ms_total = torch.tensor([t0.elapsed_time(t1)], device=dev)
+    if world > 1:
+        dist.all_reduce(ms_total, op=dist.ReduceOp.MAX)
+    ms_step = float(ms_total) / args.steps
+    step_bytes = fwd_bytes(M, N) + bwd_bytes(M, N)
+    value = world * step_bytes / ms_step / 1e6
+    kms = tl.mean_ms()
+    launches = tl.count() - (len(tl.spans.get("dw_allreduce", [])))
+
+    # ---- end to end through the public API with host buffers (rank-local, then max over ranks) ----
+    quack_rmsnorm = rn.rmsnorm
+    hx, hres, hdout = (t.cpu().pin_memory() for t in (x, res, dout))
+    hw = w.cpu().pin_memory()
+    h_out, h_dx = (torch.empty(M, N, dtype=bf).pin_memory() for _ in range(2))
+    h_dw = torch.empty(N, dtype=bf).pin_memory()
+    dxg, dresg, dwg = (torch.empty_like(x), torch.empty_like(x), torch.empty_like(w))
+
+    def e2e_step():
+        xd = dxg.copy_(hx, non_blocking=True).requires_grad_()
+        rd = dresg.copy_(hres, non_blocking=True).requires_grad_()
+        wd = dwg.copy_(hw, non_blocking=True).requires_grad_()
+        dd = dout.copy_(hdout, non_blocking=True)
+        o = quack_rmsnorm(xd, wd, residual=rd, eps=EPS)
+        o.backward(dd)
+        dwv = wd.grad
+        if world > 1:
+            d32 = dwv.float()
+            dist.all_reduce(d32)
+            dwv = d32.to(bf)
+        h_out.copy_(o.detach(), non_blocking=True)
+        h_dx.copy_(xd.grad, non_blocking=True)  # dresidual is the same tensor
+        h_dw.copy_(dwv, non_blocking=True)
+        for t in (dxg, dresg, dwg):
+            t.grad = None
+            t.requires_grad_(False)
+
+    e2e_steps = max(3, min(args.steps, 5))
+    for _ in range(2):
+        e2e_step()
+    sync_all()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record()
+    sync_all()
+    e2e_ms = torch.tensor([e0.elapsed_time(e1) / e2e_steps], device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e = {"value": world * step_bytes / float(e2e_ms) / 1e6, "unit": "GB/s",
+           "h2d_bytes_per_step": 3 * M * N * 2 + N * 2, "d2h_bytes_per_step": 2 * M * N * 2 + N * 2,
+           "ms_per_step": float(e2e_ms),
+           "api": "quack.rmsnorm(x, w, residual=res) + backward through autograd; pinned host buffers; "
+                  "x, residual, dout, weight copied in; out, dx (= dresidual), dw copied back"}
+    del hx, hres, hdout, h_out, h_dx
+
+    if rank == 0:
+        fwd_ms = kms["rmsnorm_fwd"]
+        fwd_gbs = fwd_bytes(M, N) / fwd_ms / 1e6
+        kernels = {
+            "rmsnorm_fwd": {"ms": round(fwd_ms, 4), "gbs": round(fwd_gbs, 1),
+                            "frac_of_measured_peak": round(fwd_gbs / peak, 4), "bytes": fwd_bytes(M, N)},
+            "rmsnorm_bwd": {"ms": round(kms["rmsnorm_bwd"], 4),
+                            "gbs": round(bwd_bytes(M, N) / kms["rmsnorm_bwd"] / 1e6, 1),
+                            "frac_of_measured_peak": round(bwd_bytes(M, N) / kms["rmsnorm_bwd"] / 1e6 / peak, 4),
+                            "bytes": bwd_bytes(M, N)},
+            "dw_colsum": {"ms": round(kms["dw_colsum"], 4)},
+        }
+        if "dw_allreduce" in kms:
+            kernels["dw_allreduce_nccl"] = {"ms": round(kms["dw_allreduce"], 4)}
+        if not args.no_suite:
+            try:
+                del x, res, dout, out, res_out, dx
+                torch.cuda.empty_cache()
+                kernels.update(suite(dev, peak))
+            except Exception as exc:  # the headline line must still be printed
+                kernels["suite_error"] = repr(exc)
+        cpu = cpu_baseline(rows=2048) if world == 1 else None
+        line = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "pct_of_8TBs": round(100 * value / (world * NOMINAL_HBM_GBS), 2),
+            "config": {"workload": WORKLOAD, "rows_per_gpu": M, "N": N,
+                       "step": "rmsnorm_fwd kernel + rmsnorm_bwd kernel + dw column-sum kernel"
+                               + (" + NCCL all-reduce of fp32 dw" if world > 1 else ""),
+                       "l2": "inputs exceed L2: every streamed tensor is 512 MiB (L2 is 126 MB)",
+                       "bytes_per_step_per_gpu": step_bytes, "num_partials": P},
+            "roofline": {"bound": "hbm", "kernel": "norm_fwd_kernel (RMSNorm forward)",
+                         "achieved": round(fwd_gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(fwd_gbs / peak, 4), "peak_source": peak_src,
+                         "traffic": None},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": launches,
+            "clocks": clocks,
+            "kernels": kernels,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-suite", action="store_true", help="skip the per-kernel sweep of the other configurations")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -162,7 +162,16 @@ inline int plan_rows(const char* op, int64_t N, int vec, const ElemCaps& caps,
     if (tpr < 32) tpr = 32;
     threads = tpr;
   }
-  const int K = next_pow2(ceil_div(cpc, tpr));
+  int K = next_pow2(ceil_div(cpc, tpr));
+  if (threads != 0 && cfg.threads_per_row != 0) {
+    // An explicit row-group width too narrow for the registers is widened (the override is a
+    // performance hint; results do not depend on it).
+    while (K > max_k(caps, threads > tpr ? threads : tpr, vec) && tpr < 1024) {
+      tpr <<= 1;
+      if (threads < tpr) threads = tpr;
+      K = next_pow2(ceil_div(cpc, tpr));
+    }
+  }
   if (threads == 0) {
     // Several rows per CTA for short rows, as long as the per-thread footprint allows the size.
     threads = tpr > 32 ? tpr : 32;

@@ -1,0 +1,68 @@
+"""Worker of the multi-GPU test (one process per GPU, NCCL): row-sharded RMSNorm backward with the
+dw / db all-reduce and vocabulary-sharded cross-entropy, each checked against the unsharded CPU
+oracle on rank 0's copy of the global problem."""
+
+import os
+import sys
+from pathlib import Path
+
+import torch
+import torch.distributed as dist
+
+ROOT = Path(__file__).resolve().parents[1]
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "tests"))
+
+import oracle  # noqa: E402
+from quack_flydsl_b200 import sharded  # noqa: E402
+
+
+def main():
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    torch.cuda.set_device(int(os.environ["LOCAL_RANK"]))
+    dist.init_process_group("nccl")
+    dev = torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator().manual_seed(0)
+    M, N = 1024, 8192
+    x = torch.randn(M, N, generator=g).bfloat16()
+    dout = torch.randn(M, N, generator=g).bfloat16()
+    w = (1 + 0.1 * torch.randn(N, generator=g)).bfloat16()
+    rstd = oracle.rmsnorm_rstd_ref(x)
+    b, e = sharded.row_shard(M, rank, world)
+    dx, dw, db, _ = sharded.norm_bwd_row_sharded(x[b:e].to(dev), w.to(dev), dout[b:e].to(dev),
+                                                 rstd[b:e].to(dev), has_bias=True)
+    dx_ref, dw_ref, db_ref = oracle.rmsnorm_bwd_ref(x, w, dout, rstd, has_bias=True)
+    tol = 2 * 2 ** -8
+    ok = torch.allclose(dx.float().cpu(), dx_ref[b:e].bfloat16().float(), atol=tol * float(dx_ref.abs().max()), rtol=1e-2)
+    ok &= torch.allclose(dw.float().cpu(), dw_ref.bfloat16().float(), atol=tol * float(dw_ref.abs().max()), rtol=1e-2)
+    ok &= torch.allclose(db.float().cpu(), db_ref.bfloat16().float(), atol=tol * float(db_ref.abs().max()), rtol=1e-2)
+    # every rank must hold bit-identical parameter gradients
+    gathered = [torch.empty_like(dw) for _ in range(world)]
+    dist.all_gather(gathered, dw)
+    ok &= all(torch.equal(gathered[0], t) for t in gathered)
+
+    Mc, Nc = 256, 128256
+    logits = (2 * torch.randn(Mc, Nc, generator=g)).bfloat16()
+    target = torch.randint(0, Nc, (Mc,), generator=g)
+    target[::9] = -100
+    cb, ce_ = sharded.vocab_shard(Nc, rank, world)
+    xs = logits[:, cb:ce_].contiguous().to(dev).requires_grad_()
+    loss = sharded.cross_entropy_vocab_parallel(xs, target.to(dev), cb, reduction="mean")
+    loss.backward()
+    loss_ref, lse_ref = oracle.cross_entropy_ref(logits, target)
+    nvalid = int((target != -100).sum())
+    ok &= torch.allclose(loss.detach().cpu(), loss_ref.sum() / nvalid, atol=0, rtol=1e-5)
+    dx_ref = oracle.cross_entropy_bwd_ref(logits[:, cb:ce_].float(), target, torch.full((Mc,), 1.0 / nvalid),
+                                          lse_ref, col_offset=cb)
+    ok &= bool((oracle.bf16_ulp_diff(xs.grad, dx_ref.bfloat16()) <= 2).all())
+    flag = torch.tensor([1 if ok else 0], device=dev)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    dist.barrier()
+    if rank == 0:
+        print("DIST_WORKER_PASS" if int(flag) == 1 else "DIST_WORKER_FAIL", flush=True)
+    dist.destroy_process_group()
+    sys.exit(0 if int(flag) == 1 else 1)
+
+
+if __name__ == "__main__":
+    main()

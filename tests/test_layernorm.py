@@ -1,0 +1,151 @@
+"""GPU parity tests of LayerNorm forward / backward against the CPU oracle, after the reference's
+tests/test_layernorm.py (parametrisation, tolerances, ragged-N known-answer regression)."""
+
+import importlib
+
+import pytest
+import torch
+
+import oracle
+from _util import assert_close_to_oracle
+
+pytestmark = pytest.mark.gpu
+
+ln = importlib.import_module("quack_flydsl_b200.layernorm")
+DEV = "cuda"
+
+
+@pytest.mark.parametrize("has_bias", [True, False])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("N", [256, 512, 760, 1024, 1128, 2048, 4096, 8192, 16384, 32768, 65536,
+                               131072, 262144])
+@pytest.mark.parametrize("M", [1, 37, 199, 4096])
+def test_layernorm_forward_backward(M, N, dtype, has_bias):
+    if M == 4096 and N > 16384:
+        pytest.skip("covered by smaller M and by the full-size configuration test")
+    if M == 37 and N not in (256, 1128, 32768):
+        pytest.skip("same tile choice as M=199")
+    eps = 1e-6
+    x = torch.randn(M, N, device=DEV, dtype=dtype)
+    w = torch.randn(N, device=DEV, dtype=torch.float32)
+    out, rstd, mean = ln.layernorm_fwd(x, w, eps=eps, return_rstd=True, return_mean=True)
+    assert out.shape == x.shape and out.dtype == dtype
+    assert rstd.shape == (M,) and rstd.dtype == torch.float32
+    assert mean.shape == (M,) and mean.dtype == torch.float32
+    xc, wc = x.cpu(), w.cpu()
+    ref = oracle.layernorm_ref(xc.float(), wc, eps=eps)
+    assert_close_to_oracle(out, ref, dtype, atol={torch.float32: 1e-4}.get(dtype), what="out")
+    torch.testing.assert_close(rstd.cpu(), oracle.layernorm_rstd_ref(xc, eps=eps), atol=1e-6, rtol=1e-5)
+    torch.testing.assert_close(mean.cpu(), oracle.layernorm_mean_ref(xc), atol=1e-5, rtol=1e-5)
+    if N > 128 * 1024 and dtype == torch.float32:
+        return  # fp32 backward is limited to N <= 128K, as in the reference
+    dout = torch.randn_like(x)
+    dx, dw, db = ln.layernorm_bwd(x, w, dout, rstd, mean, has_bias=has_bias)
+    assert dx.shape == x.shape and dx.dtype == dtype
+    assert dw.shape == (N,) and dw.dtype == torch.float32
+    dx_ref, dw_ref, db_ref = oracle.layernorm_bwd_ref(xc, wc, dout.cpu(), rstd.cpu(), mean.cpu(), has_bias)
+    assert_close_to_oracle(dx, dx_ref, dtype, atol={torch.float32: 2e-4}.get(dtype), max_ulp=None, what="dx")
+    sum_atol = 5e-6 * (M ** 0.5) * 4 if dtype == torch.float32 else 1e-3 * (M ** 0.5)
+    torch.testing.assert_close(dw.cpu(), dw_ref, atol=sum_atol, rtol=1e-3)
+    if has_bias:
+        assert db.shape == (N,) and db.dtype == torch.float32
+        torch.testing.assert_close(db.cpu(), db_ref, atol=sum_atol, rtol=1e-3)
+    else:
+        assert db is None
+
+
+def test_layernorm_fwd_return_arity():
+    M, N = 37, 1024
+    x = torch.randn(M, N, device=DEV, dtype=torch.bfloat16)
+    w = torch.randn(N, device=DEV, dtype=torch.float32)
+    out_r, rstd_only = ln.layernorm_fwd(x, w, return_rstd=True, return_mean=False)
+    assert out_r.shape == x.shape and rstd_only.shape == (M,) and rstd_only.dtype == torch.float32
+    out_m, mean_only = ln.layernorm_fwd(x, w, return_rstd=False, return_mean=True)
+    assert out_m.shape == x.shape and mean_only.shape == (M,)
+    out_only = ln.layernorm_fwd(x, w)
+    assert isinstance(out_only, torch.Tensor) and out_only.shape == x.shape
+
+
+def test_layernorm_ragged_n_known_answer(norm_golden):
+    """Closed-form input of the reference's regression test (tests/test_layernorm.py:121-139):
+    padding lanes of a ragged row must not enter the variance."""
+    c = norm_golden["layernorm_ragged_known_answer"]
+    x, w = c["x"].to(DEV), c["w"].to(DEV)
+    out, rstd, mean = ln.layernorm_fwd(x, w, eps=c["eps"], return_rstd=True, return_mean=True)
+    torch.testing.assert_close(out.cpu(), oracle.layernorm_ref(c["x"], c["w"], eps=c["eps"]), atol=2e-4, rtol=1e-4)
+    torch.testing.assert_close(rstd.cpu(), oracle.layernorm_rstd_ref(c["x"], eps=c["eps"]), atol=1e-5, rtol=1e-5)
+    torch.testing.assert_close(mean.cpu(), oracle.layernorm_mean_ref(c["x"]), atol=1e-5, rtol=1e-5)
+    # and the committed outputs of the reference's own CPU functions
+    torch.testing.assert_close(out.cpu(), c["out"], atol=4e-4, rtol=1e-4)
+    torch.testing.assert_close(rstd.cpu(), c["rstd"], atol=1e-5, rtol=1e-4)
+
+
+def test_layernorm_golden_fixtures(norm_golden):
+    for c in norm_golden["layernorm"]:
+        x, w, dout = c["x"].to(DEV), c["w"].to(DEV), c["dout"].to(DEV)
+        out, rstd, mean = ln.layernorm_fwd(x, w, eps=c["eps"], return_rstd=True, return_mean=True)
+        dt = x.dtype
+        assert_close_to_oracle(out, c["out"].float(), dt, atol={torch.float32: 2e-5}.get(dt), max_ulp=1, what="out")
+        torch.testing.assert_close(rstd.cpu(), c["rstd"], atol=0, rtol=1e-5)
+        dx, dw, db = ln.layernorm_bwd(x, w, dout, rstd, mean)
+        assert_close_to_oracle(dx, c["dx"].float(), dt, atol={torch.float32: 5e-5}.get(dt), max_ulp=None, what="dx")
+        torch.testing.assert_close(dw.cpu(), c["dw"], atol=1e-3, rtol=1e-3)
+        torch.testing.assert_close(db.cpu(), c["db"], atol=1e-3, rtol=1e-3)
+
+
+def test_layernorm_autograd_bf16_params_config_shape():
+    """Shape family of the BASELINE LayerNorm configuration (bf16 x, weight and bias, eps 1e-5,
+    x ~ N(0.5, 1)) through the autograd wrapper, on a row slice the CPU oracle handles."""
+    M, N, eps = 2048, 4096, 1e-5
+    d = oracle.make_config_inputs("c3", rows=M, device=DEV)
+    x = d["x"].requires_grad_()
+    w = d["weight"].requires_grad_()
+    b = d["bias"].requires_grad_()
+    out = ln.layernorm(x, w, b, eps=eps)
+    out.backward(d["dout"])
+    xc, wc, bc = x.detach().cpu(), w.detach().cpu(), b.detach().cpu()
+    assert_close_to_oracle(out.detach(), oracle.layernorm_ref(xc.float(), wc, bias=bc, eps=eps), torch.bfloat16, what="out")
+    rstd, mean = oracle.layernorm_rstd_ref(xc, eps=eps), oracle.layernorm_mean_ref(xc)
+    dx_ref, dw_ref, db_ref = oracle.layernorm_bwd_ref(xc, wc, d["dout"].cpu(), rstd, mean)
+    assert_close_to_oracle(x.grad, dx_ref, torch.bfloat16, max_ulp=None, what="dx")
+    assert w.grad.dtype == torch.bfloat16 and b.grad.dtype == torch.bfloat16
+    for g, r in ((w.grad, dw_ref), (b.grad, db_ref)):
+        torch.testing.assert_close(g.float().cpu(), r.bfloat16().float(),
+                                   atol=2 * 2 ** -8 * float(r.abs().max()), rtol=1e-2)
+
+
+def test_layernorm_full_size_config_properties():
+    """BASELINE configuration bf16 [65536, 4096] at full size: statistics against the fp32 formulas
+    on the GPU, outputs through size-independent properties."""
+    M, N, eps = 65536, 4096, 1e-5
+    g = torch.Generator(device=DEV).manual_seed(0)
+    x = (0.5 + torch.randn(M, N, device=DEV, generator=g)).bfloat16()
+    w = (1 + 0.1 * torch.randn(N, device=DEV, generator=g)).bfloat16()
+    b = (0.1 * torch.randn(N, device=DEV, generator=g)).bfloat16()
+    dout = torch.randn(M, N, device=DEV, generator=g).bfloat16()
+    out = torch.empty_like(x)
+    rstd = torch.empty(M, device=DEV)
+    mean = torch.empty(M, device=DEV)
+    ln._rmsnorm_fwd(x, w, out, b, rstd, mean, None, None, eps, True)
+    torch.testing.assert_close(mean, oracle.layernorm_mean_ref(x), atol=1e-6, rtol=1e-5)
+    torch.testing.assert_close(rstd, oracle.layernorm_rstd_ref(x, eps=eps), atol=0, rtol=1e-5)
+    assert_close_to_oracle(out[:4096], oracle.layernorm_ref(x[:4096].float(), w, bias=b, eps=eps), torch.bfloat16, what="out")
+    dx, dw, db = ln._layernorm_bwd_impl(x, w, dout, rstd, mean, True, torch.bfloat16)
+    # LayerNorm gradient rows sum to zero and are orthogonal to the centred input
+    s = dx.float().sum(-1)
+    assert (s.abs() <= 2e-3 * dx.float().abs().sum(-1)).all()
+    torch.testing.assert_close(db.float(), dout.float().sum(0).bfloat16().float(), atol=4.0, rtol=2e-2)
+    dx_ref, _, _ = oracle.layernorm_bwd_ref(x[:2048], w, dout[:2048], rstd[:2048], mean[:2048])
+    assert_close_to_oracle(dx[:2048], dx_ref, torch.bfloat16, max_ulp=None, what="dx")
+    # bitwise reproducible dw / db
+    dx2, dw2, db2 = ln._layernorm_bwd_impl(x, w, dout, rstd, mean, True, torch.bfloat16)
+    assert torch.equal(dw, dw2) and torch.equal(db, db2) and torch.equal(dx, dx2)
+
+
+def test_layernorm_empty():
+    x = torch.empty(0, 1024, device=DEV, dtype=torch.bfloat16)
+    w = torch.randn(1024, device=DEV)
+    out, rstd, mean = ln.layernorm_fwd(x, w, return_rstd=True, return_mean=True)
+    assert out.shape == (0, 1024)
+    dx, dw, db = ln.layernorm_bwd(x, w, torch.empty_like(x), rstd, mean)
+    assert (dw == 0).all() and (db == 0).all()
