@@ -33,10 +33,14 @@ def assert_close_to_oracle(got, ref_f32, dtype, atol=None, rtol=1e-3, max_ulp=2,
             d = oracle.bf16_ulp_diff(g, w)
             bad = d > max_ulp
             if bad.any():
-                big = (w.float().abs().cpu() > 1e-30) & bad
+                # An output that is itself the result of a cancellation (x_hat * w + b ~ 0, or
+                # x - mean ~ 0) carries the fp32 rounding noise of its operands, which can be many
+                # ulps of the tiny result: such elements are held to an absolute floor instead.
+                floor = 1e-5 * max(1.0, float(ref.abs().max()))
+                big = bad & ((g.float() - w.float()).abs().cpu() > floor)
                 assert not big.any(), (
                     f"{what}: {int(big.sum())} elements differ by more than {max_ulp} bf16 ulp "
-                    f"(max {int(d.max())})")
+                    f"(max {int(d[big].max())}) and by more than {floor:.1e}")
     else:
         a = ATOL[dtype] if atol is None else atol
         if atol is None and dtype != torch.float32:
