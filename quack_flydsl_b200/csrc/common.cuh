@@ -33,6 +33,24 @@ __device__ __forceinline__ float fast_exp2(float x) {
 }
 __device__ __forceinline__ float neg_inf() { return __int_as_float(0xff800000); }
 
+// exp2 offset for a running maximum m, split so that 2^(x*log2e + hi) * 2^lo == exp(x - m)
+// up to the rounding of one fused multiply-add.
+struct ExpOffset {
+  float hi, lo;
+};
+__device__ __forceinline__ ExpOffset exp_offset(float m) {
+  ExpOffset o;
+  if (m == neg_inf()) {
+    o.hi = 0.0f;
+    o.lo = 0.0f;
+  } else {
+    o.hi = -m * kLog2e;
+    o.lo = fmaf(-m, kLog2e, -o.hi);
+  }
+  return o;
+}
+
+
 // ---------------------------------------------------------------------------------------------
 // raw global / shared memory access of 2, 4, 8 or 16 bytes
 // ---------------------------------------------------------------------------------------------
@@ -439,12 +457,13 @@ struct MaxOp {
 
 constexpr int kMaxWarps = 32;
 constexpr int kMaxCluster = 16;
-constexpr int kRedStages = 2;  // independent reductions per row tile
+constexpr int kClusterSlots = 128;  // warp partials of a whole cluster exchanged in one step
+constexpr int kRedStages = 2;       // independent reductions per row tile
 // Shared-memory scratch of the reductions.  Indexed [stage][parity] so that consecutive row tiles
 // of a persistent CTA never overwrite a buffer a slower warp may still be reading.
 struct __align__(16) ReduceScratch {
   float2 warp_part[kRedStages][2][kMaxWarps];
-  float2 cta_part[kRedStages][2][kMaxCluster];
+  float2 cta_part[kRedStages][2][kClusterSlots];
 };
 
 // Position of a thread in the row-tile geometry of its CTA.
@@ -493,6 +512,24 @@ __device__ __forceinline__ float2 row_reduce(float2 v, const RowGeom& g, ReduceS
   } else {
     for (int o = g.tpr >> 1; o > 0; o >>= 1) v = Op::combine(v, shfl_xor_f2(v, o));
   }
+  if (g.cluster_n > 1) {
+    // 2+3 (cluster): every warp pushes its partial into slot [crank * warps + warp] of every
+    //    CTA's buffer through distributed shared memory, ONE cluster barrier publishes the
+    //    stores (it also orders the warps of this CTA), and every warp folds all slots in the
+    //    same order, so all CTAs obtain bit-identical results.
+    const int nslots = g.warps_per_row * g.cluster_n;
+    if (nslots <= kClusterSlots) {
+      float2* buf = s.cta_part[stage][parity];
+      if (g.lane < g.cluster_n)
+        st_shared_cluster_f2(&buf[g.crank * g.warps_per_row + g.warp_in_row], g.lane, v);
+      cluster_sync_all();
+      float2 acc = Op::identity();
+      for (int i = g.lane; i < nslots; i += 32) acc = Op::combine(acc, buf[i]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc = Op::combine(acc, shfl_xor_f2(acc, o));
+      return acc;
+    }
+  }
   // 2. across the warps of the row group
   if (g.warps_per_row > 1) {
     float2* buf = s.warp_part[stage][parity];
@@ -502,9 +539,9 @@ __device__ __forceinline__ float2 row_reduce(float2 v, const RowGeom& g, ReduceS
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v = Op::combine(v, shfl_xor_f2(v, o));
   }
-  // 3. across the CTAs of the cluster: every CTA pushes its partial into slot [crank] of every
-  //    CTA's buffer, a cluster barrier publishes the stores, and all CTAs fold the slots in rank
-  //    order (so all of them obtain bit-identical results).
+  // 3. across the CTAs of the cluster (only when the one-step exchange above does not fit):
+  //    every CTA pushes its partial into slot [crank] of every CTA's buffer, a cluster barrier
+  //    publishes the stores, and all CTAs fold the slots in rank order.
   if (g.cluster_n > 1) {
     float2* buf = s.cta_part[stage][parity];
     if (threadIdx.x < g.cluster_n) st_shared_cluster_f2(&buf[g.crank], threadIdx.x, v);

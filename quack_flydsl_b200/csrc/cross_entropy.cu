@@ -19,23 +19,6 @@ struct CeFwdParams {
 
 constexpr int kCeUnroll = 4;  // chunks in flight per thread and loop iteration
 
-// exp2 offset for a running maximum m, split so that 2^(x*log2e + hi) * 2^lo == exp(x - m)
-// up to the rounding of one fused multiply-add.
-struct ExpOffset {
-  float hi, lo;
-};
-__device__ __forceinline__ ExpOffset exp_offset(float m) {
-  ExpOffset o;
-  if (m == neg_inf()) {
-    o.hi = 0.0f;
-    o.lo = 0.0f;
-  } else {
-    o.hi = -m * kLog2e;
-    o.lo = fmaf(-m, kLog2e, -o.hi);
-  }
-  return o;
-}
-
 template <int DT, int VEC>
 __global__ void __launch_bounds__(512) ce_fwd_kernel(const CeFwdParams p) {
   __shared__ ReduceScratch scratch;
@@ -133,9 +116,11 @@ __global__ void __launch_bounds__(512) ce_fwd_kernel(const CeFwdParams p) {
 struct CeBwdParams {
   qb_ce_bwd_args a;
   int tpr, rows_per_cta;
-  int cols_per_block;  // tpr * kCeUnroll * VEC
+  int cols_per_block;  // tpr * kCeBwdUnroll * VEC
   int64_t num_tiles;
 };
+
+constexpr int kCeBwdUnroll = 8;  // chunks per thread and column block
 
 template <int DT, int VEC>
 __global__ void __launch_bounds__(512) ce_bwd_kernel(const CeBwdParams p) {
@@ -143,47 +128,52 @@ __global__ void __launch_bounds__(512) ce_bwd_kernel(const CeBwdParams p) {
   const int t = threadIdx.x & (p.tpr - 1);
   const int r = threadIdx.x / p.tpr;
   const int N = static_cast<int>(a.N);
-  const int cb0 = blockIdx.y * p.cols_per_block;
+  const int colbase = blockIdx.y * p.cols_per_block + t * VEC;
+  const int cstride = p.tpr * VEC;
+  // chunks of this thread inside the row: u < nu
+  const int nu = colbase < N ? min(kCeBwdUnroll, (N - colbase + cstride - 1) / cstride) : 0;
   for (int64_t tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
     const int64_t row = tile * p.rows_per_cta + r;
     const bool row_ok = row < a.M;
-    int col[kCeUnroll];
-    bool ok[kCeUnroll];
-    uint32_t raw[kCeUnroll][RawWords<DT, VEC>::value];
+    const int nur = row_ok ? nu : 0;
+    uint32_t raw[kCeBwdUnroll][RawWords<DT, VEC>::value];
 #pragma unroll
-    for (int u = 0; u < kCeUnroll; ++u) {
-      col[u] = cb0 + (u * p.tpr + t) * VEC;
-      ok[u] = row_ok && col[u] < N;
-      load_chunk_raw<DT, VEC>(raw[u], a.x, row * a.x_row_stride + col[u], a.x_dtype, ok[u]);
-    }
+    for (int u = 0; u < kCeBwdUnroll; ++u)
+      load_chunk_raw<DT, VEC>(raw[u], a.x, row * a.x_row_stride + colbase + u * cstride, a.x_dtype,
+                              u < nur);
     // Row scalars (the same addresses for every thread of the row group: broadcast loads).
     float gscale = 0.0f;  // dloss * w[target], 0 for ignored rows
     float lse = 0.0f;
-    int64_t tcol = -1;  // local column of the target, -1 if none
+    int tcol = -1;  // local column of the target, -1 if none inside this shard
     if (row_ok) {
       const int64_t tgt = load_index(a.target, row, a.target_dtype);
       lse = a.lse[row];
       if (tgt != a.ignore_index) {
         gscale = a.dloss != nullptr ? a.dloss[row * a.dloss_stride] : 1.0f;
         if (a.weight != nullptr) gscale *= load_scalar(a.weight, tgt, a.weight_dtype);
-        tcol = tgt - a.col_offset;
+        const int64_t local = tgt - a.col_offset;
+        if (local >= 0 && local < a.N) tcol = static_cast<int>(local);
       }
     }
     // exp(x - lse) = 2^(x*log2e + hi) * 2^lo; the row-constant 2^lo is folded into the scale.
     const ExpOffset off = exp_offset(lse);
     const float pscale = fast_exp2(off.lo) * gscale;
 #pragma unroll
-    for (int u = 0; u < kCeUnroll; ++u) {
-      if (ok[u]) {
+    for (int u = 0; u < kCeBwdUnroll; ++u) {
+      if (u < nur) {
+        const int c = colbase + u * cstride;
         float v[VEC], d[VEC];
         unpack_chunk<DT, VEC>(v, raw[u], a.x_dtype);
 #pragma unroll
-        for (int i = 0; i < VEC; ++i) {
-          const float e = fast_exp2(fmaf(v[i], kLog2e, off.hi));
-          const float hot = (static_cast<int64_t>(col[u] + i) == tcol) ? gscale : 0.0f;
-          d[i] = fmaf(e, pscale, -hot);
+        for (int i = 0; i < VEC; ++i) d[i] = fast_exp2(fmaf(v[i], kLog2e, off.hi)) * pscale;
+        // one-hot term: at most one element of one chunk of the row
+        const unsigned rel = static_cast<unsigned>(tcol - c);
+        if (rel < static_cast<unsigned>(VEC)) {
+#pragma unroll
+          for (int i = 0; i < VEC; ++i)
+            if (rel == static_cast<unsigned>(i)) d[i] -= gscale;
         }
-        store_chunk<DT, VEC>(a.dx, row * a.dx_row_stride + col[u], d, a.dx_dtype);
+        store_chunk<DT, VEC>(a.dx, row * a.dx_row_stride + c, d, a.dx_dtype);
       }
     }
   }
@@ -268,14 +258,14 @@ static int run_ce_bwd(const qb_ce_bwd_args& a, cudaStream_t st) {
   if (!is_pow2(threads) || threads < 32 || threads > 512)
     return set_error(QB_ERR_INVALID, "ce_bwd: bad num_threads %d", threads);
   const int64_t chunks = a.N / vec;
-  int tpr = next_pow2(ceil_div(chunks, kCeUnroll));
+  int tpr = next_pow2(ceil_div(chunks, kCeBwdUnroll));
   if (tpr < 8) tpr = 8;
   if (tpr > threads) tpr = threads;
   CeBwdParams p;
   p.a = a;
   p.tpr = tpr;
   p.rows_per_cta = threads / tpr;
-  p.cols_per_block = tpr * kCeUnroll * vec;
+  p.cols_per_block = tpr * kCeBwdUnroll * vec;
   p.num_tiles = ceil_div(a.M, p.rows_per_cta);
   const int64_t col_blocks = ceil_div(a.N, p.cols_per_block);
   if (col_blocks > 65535) return set_error(QB_ERR_UNSUPPORTED, "ce_bwd: N too large");

@@ -82,12 +82,13 @@ struct ElemCaps {
   int c256;   // CTAs of <= 256 threads
   int c512;   // CTAs of 257..512 threads
   int c1024;  // CTAs of 513..1024 threads
+  int kmax = 0;  // largest instantiated K; 0 = default (16 for vec <= 4, else 8)
   int at(int threads) const { return threads > 512 ? c1024 : (threads > 256 ? c512 : c256); }
 };
 
 // Largest chunks-per-thread K (a power of two; 16 only exists for vec <= 4) for a CTA size.
 inline int max_k(const ElemCaps& caps, int threads, int vec) {
-  const int kmax = vec <= 4 ? 16 : 8;
+  const int kmax = caps.kmax > 0 ? caps.kmax : (vec <= 4 ? 16 : 8);
   int k = 1;
   while (k * 2 <= kmax && k * 2 * vec <= caps.at(threads)) k <<= 1;
   return (k * vec <= caps.at(threads)) ? k : 0;

@@ -39,8 +39,98 @@ __device__ __forceinline__ void cp_async_wait_dyn(int n) {
   }
 }
 
+// Element-wise helpers on VEC-wide register arrays.  Pairs of lanes go through the packed
+// fp32x2 instructions of sm_100 (fma.rn.f32x2 and friends), which halves the issue slots of the
+// arithmetic: this kernel is bound by instruction issue as much as by HBM.
+template <int VEC>
+__device__ __forceinline__ void vmul(float (&o)[VEC], const float (&a)[VEC], const float (&b)[VEC]) {
+  if constexpr (VEC >= 2) {
+#pragma unroll
+    for (int i = 0; i < VEC; i += 2) {
+      const float2 r = __fmul2_rn(make_float2(a[i], a[i + 1]), make_float2(b[i], b[i + 1]));
+      o[i] = r.x; o[i + 1] = r.y;
+    }
+  } else {
+    o[0] = a[0] * b[0];
+  }
+}
+// o = a * b + c
+template <int VEC>
+__device__ __forceinline__ void vfma(float (&o)[VEC], const float (&a)[VEC], const float (&b)[VEC],
+                                     const float (&c)[VEC]) {
+  if constexpr (VEC >= 2) {
+#pragma unroll
+    for (int i = 0; i < VEC; i += 2) {
+      const float2 r = __ffma2_rn(make_float2(a[i], a[i + 1]), make_float2(b[i], b[i + 1]),
+                                  make_float2(c[i], c[i + 1]));
+      o[i] = r.x; o[i + 1] = r.y;
+    }
+  } else {
+    o[0] = fmaf(a[0], b[0], c[0]);
+  }
+}
+// o = a * s + c with a scalar s
+template <int VEC>
+__device__ __forceinline__ void vfma_s(float (&o)[VEC], const float (&a)[VEC], float s,
+                                       const float (&c)[VEC]) {
+  if constexpr (VEC >= 2) {
+    const float2 s2 = make_float2(s, s);
+#pragma unroll
+    for (int i = 0; i < VEC; i += 2) {
+      const float2 r = __ffma2_rn(make_float2(a[i], a[i + 1]), s2, make_float2(c[i], c[i + 1]));
+      o[i] = r.x; o[i + 1] = r.y;
+    }
+  } else {
+    o[0] = fmaf(a[0], s, c[0]);
+  }
+}
+// o = a * s + t with scalars s, t
+template <int VEC>
+__device__ __forceinline__ void vfma_ss(float (&o)[VEC], const float (&a)[VEC], float s, float t) {
+  if constexpr (VEC >= 2) {
+    const float2 s2 = make_float2(s, s), t2 = make_float2(t, t);
+#pragma unroll
+    for (int i = 0; i < VEC; i += 2) {
+      const float2 r = __ffma2_rn(make_float2(a[i], a[i + 1]), s2, t2);
+      o[i] = r.x; o[i + 1] = r.y;
+    }
+  } else {
+    o[0] = fmaf(a[0], s, t);
+  }
+}
+template <int VEC>
+__device__ __forceinline__ void vadd(float (&o)[VEC], const float (&a)[VEC], const float (&b)[VEC]) {
+  if constexpr (VEC >= 2) {
+#pragma unroll
+    for (int i = 0; i < VEC; i += 2) {
+      const float2 r = __fadd2_rn(make_float2(a[i], a[i + 1]), make_float2(b[i], b[i + 1]));
+      o[i] = r.x; o[i + 1] = r.y;
+    }
+  } else {
+    o[0] = a[0] + b[0];
+  }
+}
+template <int VEC>
+__device__ __forceinline__ void vadd_s(float (&o)[VEC], const float (&a)[VEC], float s) {
+  if constexpr (VEC >= 2) {
+    const float2 s2 = make_float2(s, s);
+#pragma unroll
+    for (int i = 0; i < VEC; i += 2) {
+      const float2 r = __fadd2_rn(make_float2(a[i], a[i + 1]), s2);
+      o[i] = r.x; o[i + 1] = r.y;
+    }
+  } else {
+    o[0] = a[0] + s;
+  }
+}
+
 // DT: dtype shared by x / dout / dx (/ dresidual_out / dresidual) or kDynDT.
 // LN: LayerNorm (mean subtraction, second row statistic).  DB: accumulate db.
+//
+// Per row, with xc = x - mean (mean = 0 for RMSNorm), t = dout * w, S1 = sum(xc * t), S2 = sum(t):
+//   dx = t * a + xc * b + c      a = rstd, b = -rstd^3 * S1 / N, c = -rstd * S2 / N (0 for RMSNorm)
+//   dw += (dout * xc) * rstd     db += dout
+// which is (wdy - xhat * mean(xhat * wdy) - mean(wdy)) * rstd with the row constants pulled out.
 template <int DT, int VEC, int K, bool LN, bool DB>
 __global__ void __launch_bounds__((K * VEC <= 8) ? 1024 : ((K * VEC <= 16) ? 512 : 256))
 norm_bwd_kernel(const NormBwdParams p) {
@@ -59,14 +149,11 @@ norm_bwd_kernel(const NormBwdParams p) {
   const float inv_n = 1.0f / static_cast<float>(N);
   const bool has_dres_out = a.dresidual_out != nullptr;
 
-  int col[K];
-  bool cok[K];
-#pragma unroll
-  for (int k = 0; k < K; ++k) {
-    const int local = (k * p.tpr + g.t) * VEC;
-    cok[k] = local < ncols;
-    col[k] = col0 + local;
-  }
+  // Chunk k of this thread starts at column colbase + k * cstride and exists iff k < nk.
+  const int colbase = col0 + g.t * VEC;
+  const int cstride = p.tpr * VEC;
+  const int nchunks = ncols > 0 ? ncols / VEC : 0;
+  const int nk = nchunks > g.t ? min(K, (nchunks - g.t + p.tpr - 1) / p.tpr) : 0;
 
   // Weight (+ offset) for this thread's columns, fp32, held for the whole launch.
   float w[K][VEC];
@@ -74,7 +161,8 @@ norm_bwd_kernel(const NormBwdParams p) {
 #pragma unroll
   for (int k = 0; k < K; ++k) {
     if (a.weight != nullptr) {
-      load_chunk<kDynDT, VEC, false>(w[k], a.weight, wrow + col[k], a.weight_dtype, cok[k]);
+      load_chunk<kDynDT, VEC, false>(w[k], a.weight, wrow + colbase + k * cstride, a.weight_dtype,
+                                     k < nk);
 #pragma unroll
       for (int i = 0; i < VEC; ++i) w[k][i] += a.weight_offset;
     } else {
@@ -96,9 +184,10 @@ norm_bwd_kernel(const NormBwdParams p) {
   const int64_t P = gridDim.x / p.cluster_n;
   const int64_t pidx = blockIdx.x / p.cluster_n;
   const size_t stage_bytes = static_cast<size_t>(p.n_in) * K * nthreads * kSlot;
+  const size_t in_bytes = static_cast<size_t>(K) * nthreads * kSlot;  // one input of one stage
+  unsigned char* const my_slot0 = smem_raw + static_cast<size_t>(threadIdx.x) * kSlot;
   auto slot_ptr = [&](int stage, int j, int k) -> unsigned char* {
-    return smem_raw + stage * stage_bytes +
-           (static_cast<size_t>(j * K + k) * nthreads + threadIdx.x) * kSlot;
+    return my_slot0 + stage * stage_bytes + j * in_bytes + static_cast<size_t>(k) * nthreads * kSlot;
   };
   auto issue_tile = [&](int64_t tile, int stage) {
     if (tile < p.num_tiles) {
@@ -107,15 +196,14 @@ norm_bwd_kernel(const NormBwdParams p) {
         const int64_t row = m * a.H + h;
 #pragma unroll
         for (int k = 0; k < K; ++k) {
-          if (cok[k]) {
-            stage_chunk<DT, VEC>(slot_ptr(stage, 0, k), a.x, row * a.x_row_stride + col[k],
-                                 a.x_dtype);
-            stage_chunk<DT, VEC>(slot_ptr(stage, 1, k), a.dout, row * a.dout_row_stride + col[k],
+          if (k < nk) {
+            const int c = colbase + k * cstride;
+            stage_chunk<DT, VEC>(slot_ptr(stage, 0, k), a.x, row * a.x_row_stride + c, a.x_dtype);
+            stage_chunk<DT, VEC>(slot_ptr(stage, 1, k), a.dout, row * a.dout_row_stride + c,
                                  a.dout_dtype);
             if (has_dres_out)
               stage_chunk<DT, VEC>(slot_ptr(stage, 2, k), a.dresidual_out,
-                                   row * a.dresidual_out_row_stride + col[k],
-                                   a.dresidual_out_dtype);
+                                   row * a.dresidual_out_row_stride + c, a.dresidual_out_dtype);
           }
         }
       }
@@ -143,10 +231,10 @@ norm_bwd_kernel(const NormBwdParams p) {
     issue_tile(tile + static_cast<int64_t>(S - 1) * P, (it + S - 1) % S);
     const int stage = it % S;
     const int64_t m = tile * p.rows_per_cta + g.r;
-    const bool row_ok = m < a.M;
+    const int nkr = m < a.M ? nk : 0;  // chunks of this thread that exist in this tile
     const int64_t row = m * a.H + h;
     const float rstd = rstd_nx;
-    const float mean = mean_nx;
+    const float neg_mean = -mean_nx;
     {
       const int64_t mn = (tile + P) * p.rows_per_cta + g.r;
       if (tile + P < p.num_tiles && mn < a.M) {
@@ -156,54 +244,56 @@ norm_bwd_kernel(const NormBwdParams p) {
     }
     cp_async_wait_dyn(S - 1);  // this tile's group has landed; S-1 younger groups may be in flight
 
-    // ---- pass 1: row statistics c1 = mean(xhat * wdy), c2 = mean(wdy) ----
-    float s1 = 0.0f, s2 = 0.0f;
+    // ---- pass 1: S1 = sum(xc * t), S2 = sum(t) ----
+    float s1v[VEC], s2v[VEC];
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) { s1v[i] = 0.0f; s2v[i] = 0.0f; }
 #pragma unroll
     for (int k = 0; k < K; ++k) {
-      if (row_ok && cok[k]) {
-        float x[VEC], dy[VEC];
+      if (k < nkr) {
+        float x[VEC], dy[VEC], t[VEC];
         load_chunk_smem<DT, VEC>(x, slot_ptr(stage, 0, k), a.x_dtype);
         load_chunk_smem<DT, VEC>(dy, slot_ptr(stage, 1, k), a.dout_dtype);
-#pragma unroll
-        for (int i = 0; i < VEC; ++i) {
-          const float xhat = (LN ? (x[i] - mean) : x[i]) * rstd;
-          const float wdy = dy[i] * w[k][i];
-          s1 = fmaf(xhat, wdy, s1);
-          if constexpr (LN) s2 += wdy;
-        }
+        if constexpr (LN) vadd_s<VEC>(x, x, neg_mean);
+        vmul<VEC>(t, dy, w[k]);
+        vfma<VEC>(s1v, x, t, s1v);
+        if constexpr (LN) vadd<VEC>(s2v, s2v, t);
       }
     }
+    float s1 = 0.0f, s2 = 0.0f;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) { s1 += s1v[i]; s2 += s2v[i]; }
     if (first && p.cluster_n > 1) cluster_wait();
     first = false;
     const float2 red = row_reduce<SumOp>(make_float2(s1, s2), g, scratch, 0, parity);
     parity ^= 1;
-    const float c1 = red.x * inv_n;
-    const float c2 = LN ? red.y * inv_n : 0.0f;
+    const float ca = rstd;
+    const float cb = -rstd * rstd * rstd * red.x * inv_n;
+    const float cc = LN ? -rstd * red.y * inv_n : 0.0f;
 
     // ---- pass 2: dx, dresidual, dw / db accumulation ----
 #pragma unroll
     for (int k = 0; k < K; ++k) {
-      if (row_ok && cok[k]) {
-        float x[VEC], dy[VEC], dx[VEC];
+      if (k < nkr) {
+        const int c = colbase + k * cstride;
+        float x[VEC], dy[VEC], t[VEC], dx[VEC];
         load_chunk_smem<DT, VEC>(x, slot_ptr(stage, 0, k), a.x_dtype);
         load_chunk_smem<DT, VEC>(dy, slot_ptr(stage, 1, k), a.dout_dtype);
-#pragma unroll
-        for (int i = 0; i < VEC; ++i) {
-          const float xhat = (LN ? (x[i] - mean) : x[i]) * rstd;
-          const float wdy = dy[i] * w[k][i];
-          dx[i] = (wdy - xhat * c1 - c2) * rstd;
-          dw[k][i] = fmaf(dy[i], xhat, dw[k][i]);
-          if constexpr (DB) db[k][i] += dy[i];
-        }
+        if constexpr (LN) vadd_s<VEC>(x, x, neg_mean);
+        vmul<VEC>(t, dy, w[k]);
+        vfma_ss<VEC>(dx, t, ca, cc);      // t * a + c
+        vfma_s<VEC>(dx, x, cb, dx);       // + xc * b
+        vmul<VEC>(t, dy, x);              // dout * xc
+        vfma_s<VEC>(dw[k], t, ca, dw[k]); // dw += (dout * xc) * rstd
+        if constexpr (DB) vadd<VEC>(db[k], db[k], dy);
         if (has_dres_out) {
           float dr[VEC];
           load_chunk_smem<DT, VEC>(dr, slot_ptr(stage, 2, k), a.dresidual_out_dtype);
-#pragma unroll
-          for (int i = 0; i < VEC; ++i) dx[i] += dr[i];
+          vadd<VEC>(dx, dx, dr);
         }
-        store_chunk<DT, VEC>(a.dx, row * a.dx_row_stride + col[k], dx, a.dx_dtype);
+        store_chunk<DT, VEC>(a.dx, row * a.dx_row_stride + c, dx, a.dx_dtype);
         if (a.dresidual != nullptr)
-          store_chunk<DT, VEC>(a.dresidual, row * a.dresidual_row_stride + col[k], dx,
+          store_chunk<DT, VEC>(a.dresidual, row * a.dresidual_row_stride + c, dx,
                                a.dresidual_dtype);
       }
     }
@@ -216,12 +306,13 @@ norm_bwd_kernel(const NormBwdParams p) {
   if (p.rows_per_cta == 1) {
 #pragma unroll
     for (int k = 0; k < K; ++k) {
-      if (cok[k]) {
+      if (k < nk) {
+        const int c = colbase + k * cstride;
         if (a.dw_partial != nullptr)
-          store_chunk<QB_F32, VEC>(a.dw_partial, prow + col[k], dw[k], QB_F32);
+          store_chunk<QB_F32, VEC>(a.dw_partial, prow + c, dw[k], QB_F32);
         if constexpr (DB) {
           if (a.db_partial != nullptr)
-            store_chunk<QB_F32, VEC>(a.db_partial, prow + col[k], db[k], QB_F32);
+            store_chunk<QB_F32, VEC>(a.db_partial, prow + c, db[k], QB_F32);
         }
       }
     }
@@ -355,7 +446,7 @@ static int plan_norm_bwd(int64_t N, int vec, bool uniform, int x_dtype, bool has
   const size_t stage_bytes = (size_t)out->n_in * out->rows.K * out->rows.threads * slot;
   // Ring depth: as deep as shared memory allows (leaving room for a second CTA on the SM when
   // the stage is small), at most 4 by default.
-  const size_t budget = (size_t)dev->max_smem_optin - 2048;
+  const size_t budget = (size_t)dev->max_smem_optin - 8192;  // static reduction scratch + margin
   int stages = cfg.stages > 0 ? cfg.stages : 4;
   if (stages > kMaxStages) stages = kMaxStages;
   while (stages > 1 && stage_bytes * stages > budget) --stages;

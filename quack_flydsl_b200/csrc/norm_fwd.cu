@@ -1,9 +1,16 @@
 // RMSNorm / LayerNorm forward for sm_100a.
 //
-// One row is read from HBM exactly once into fp32 registers (128-bit coalesced loads issued back to
-// back), reduced thread -> warp -> CTA -> cluster, normalised from registers and written once.
-// Behaviour follows the reference kernel quack/rmsnorm.py:150-362 (RMSNorm.kernel; LayerNorm
-// branch :263-311) and its host stub quack/rmsnorm.py:108-148.
+// One row is read from HBM exactly once (128-bit coalesced loads issued back to back), reduced
+// thread -> warp -> CTA -> cluster, normalised from registers and written once.  Behaviour follows
+// the reference kernel quack/rmsnorm.py:150-362 (RMSNorm.kernel; LayerNorm branch :263-311) and
+// its host stub quack/rmsnorm.py:108-148.
+//
+// What bounds these kernels is the number of bytes a resident thread keeps in flight, so the row
+// is held in as few registers as possible: with a residual the fp32 sum x + residual (both packed
+// inputs are in flight at once), without one the still-packed 16-bit input words, which are
+// unpacked again by each pass over the row.  Weight and bias are copied once per CTA into
+// thread-private shared-memory slots (a thread only reads back what it copied itself, so no
+// barrier is needed) and the CTA then walks over row tiles.
 #include "common.cuh"
 #include "host_common.h"
 
@@ -16,13 +23,40 @@ struct NormFwdParams {
   int cluster_n;      // CTAs sharing a row
   int cols_per_cta;   // columns owned by one CTA of the cluster (multiple of VEC)
   int64_t num_tiles;  // ceil(M / rows_per_cta)
+  int w_slot;         // bytes of one staged weight chunk (VEC * sizeof(weight dtype)), 0 if none
+  int b_slot;         // same for bias
 };
 
+// Copies one parameter chunk (weight or bias) into this thread's shared-memory slot, keeping the
+// parameter's own element width.
+template <int VEC>
+__device__ __forceinline__ void stage_param_chunk(unsigned char* slot, const void* base,
+                                                  int64_t idx, int dt, bool pred) {
+  float v[VEC];
+  load_chunk<kDynDT, VEC, false>(v, base, idx, dt, pred);
+  if (dt == QB_F32) {
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) reinterpret_cast<float*>(slot)[i] = v[i];
+  } else {
+    uint32_t w[(VEC + 1) / 2];
+    pack16<VEC>(w, v, dt == QB_BF16);
+    if constexpr (VEC == 1) {
+      *reinterpret_cast<unsigned short*>(slot) = static_cast<unsigned short>(w[0]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < VEC / 2; ++i) reinterpret_cast<uint32_t*>(slot)[i] = w[i];
+    }
+  }
+}
+
 // DT: dtype shared by x / residual / out / residual_out, or kDynDT (per-tensor run-time dtypes).
-// VEC: elements per chunk; K: chunks per thread; LN: LayerNorm instead of RMSNorm.
-template <int DT, int VEC, int K, bool LN>
-__global__ void __launch_bounds__((K * VEC > 16) ? 512 : 1024)
+// VEC: elements per chunk; K: chunks per thread; LN: LayerNorm instead of RMSNorm;
+// RAW: keep the packed input words instead of fp32 values (no residual, static 16-bit DT only).
+template <int DT, int VEC, int K, bool LN, bool RAW>
+__global__ void __launch_bounds__(RAW ? (K * VEC > 64 ? 256 : (K * VEC > 32 ? 512 : 1024))
+                                      : (K * VEC > 16 ? 512 : 1024))
 norm_fwd_kernel(const NormFwdParams p) {
+  extern __shared__ __align__(16) unsigned char smem_params[];
   __shared__ ReduceScratch scratch;
   const qb_norm_fwd_args& a = p.a;
   const RowGeom g = make_geom(p.tpr, p.cluster_n);
@@ -30,46 +64,34 @@ norm_fwd_kernel(const NormFwdParams p) {
 
   const int N = static_cast<int>(a.N);
   const int h = blockIdx.y;
+  const int nthreads = blockDim.x;
   const int col0 = static_cast<int>(g.crank) * p.cols_per_cta;
   const int ncols = min(p.cols_per_cta, N - col0);  // columns this CTA owns (may be <= 0)
   const float inv_n = 1.0f / static_cast<float>(N);
 
-  // Column of chunk k of this thread and whether it exists.
-  int col[K];
-  bool cok[K];
-#pragma unroll
-  for (int k = 0; k < K; ++k) {
-    const int local = (k * p.tpr + g.t) * VEC;
-    cok[k] = local < ncols;
-    col[k] = col0 + local;
-  }
+  // Chunk k of this thread starts at column colbase + k * cstride and exists iff k < nk (kept as
+  // two scalars instead of per-chunk arrays to save registers).
+  const int colbase = col0 + g.t * VEC;
+  const int cstride = p.tpr * VEC;
+  const int nchunks = ncols > 0 ? ncols / VEC : 0;
+  const int nk = nchunks > g.t ? min(K, (nchunks - g.t + p.tpr - 1) / p.tpr) : 0;
+#define col(k) (colbase + (k) * cstride)
+#define cok(k) ((k) < nk)
 
-  // Weight and bias: kept in registers across row tiles when the per-thread slice is small,
-  // otherwise re-read (L1/L2 hits) after each row's reduction.
-  constexpr bool kHoistW = (K * VEC <= 8);
+  // Stage weight and bias: slot (k, tid) belongs to this thread.
   const bool has_w = a.weight != nullptr;
   const bool has_b = a.bias != nullptr;
   const int64_t wrow = static_cast<int64_t>(h) * N;
-  float wr[kHoistW ? K : 1][VEC];
-  float br[kHoistW ? K : 1][VEC];
-  if constexpr (kHoistW) {
+  unsigned char* w_smem = smem_params;
+  unsigned char* b_smem = smem_params + static_cast<size_t>(K) * nthreads * p.w_slot;
 #pragma unroll
-    for (int k = 0; k < K; ++k) {
-      if (has_w) {
-        load_chunk<kDynDT, VEC, false>(wr[k], a.weight, wrow + col[k], a.weight_dtype, cok[k]);
-#pragma unroll
-        for (int i = 0; i < VEC; ++i) wr[k][i] += a.weight_offset;
-      } else {
-#pragma unroll
-        for (int i = 0; i < VEC; ++i) wr[k][i] = 1.0f;
-      }
-      if (has_b) {
-        load_chunk<kDynDT, VEC, false>(br[k], a.bias, wrow + col[k], a.bias_dtype, cok[k]);
-      } else {
-#pragma unroll
-        for (int i = 0; i < VEC; ++i) br[k][i] = 0.0f;
-      }
-    }
+  for (int k = 0; k < K; ++k) {
+    if (has_w)
+      stage_param_chunk<VEC>(w_smem + (static_cast<size_t>(k) * nthreads + threadIdx.x) * p.w_slot,
+                             a.weight, wrow + col(k), a.weight_dtype, cok(k));
+    if (has_b)
+      stage_param_chunk<VEC>(b_smem + (static_cast<size_t>(k) * nthreads + threadIdx.x) * p.b_slot,
+                             a.bias, wrow + col(k), a.bias_dtype, cok(k));
   }
 
   const int64_t tile_stride = gridDim.x / p.cluster_n;
@@ -81,38 +103,45 @@ norm_fwd_kernel(const NormFwdParams p) {
     const int64_t row = m * a.H + h;
 
     // ---- load the row (all loads issued before the first use) ----
-    float v[K][VEC];
-    {
-      uint32_t rx[K][RawWords<DT, VEC>::value];
+    constexpr int kRawWords = RawWords<DT, VEC>::value;
+    uint32_t rx[RAW ? K : 1][kRawWords];
+    float v[RAW ? 1 : K][VEC];
+    if constexpr (RAW) {
 #pragma unroll
       for (int k = 0; k < K; ++k)
-        load_chunk_raw<DT, VEC>(rx[k], a.x, row * a.x_row_stride + col[k], a.x_dtype,
-                                row_ok && cok[k]);
+        load_chunk_raw<DT, VEC>(rx[k], a.x, row * a.x_row_stride + col(k), a.x_dtype,
+                                row_ok && cok(k));
+    } else {
+      uint32_t tx[K][kRawWords];
+#pragma unroll
+      for (int k = 0; k < K; ++k)
+        load_chunk_raw<DT, VEC>(tx[k], a.x, row * a.x_row_stride + col(k), a.x_dtype,
+                                row_ok && cok(k));
       if (a.residual != nullptr) {
-        uint32_t rr[K][RawWords<DT, VEC>::value];
+        uint32_t tr[K][kRawWords];
 #pragma unroll
         for (int k = 0; k < K; ++k)
-          load_chunk_raw<DT, VEC>(rr[k], a.residual, row * a.residual_row_stride + col[k],
-                                  a.residual_dtype, row_ok && cok[k]);
+          load_chunk_raw<DT, VEC>(tr[k], a.residual, row * a.residual_row_stride + col(k),
+                                  a.residual_dtype, row_ok && cok(k));
 #pragma unroll
         for (int k = 0; k < K; ++k) {
           float t[VEC];
-          unpack_chunk<DT, VEC>(v[k], rx[k], a.x_dtype);
-          unpack_chunk<DT, VEC>(t, rr[k], a.residual_dtype);
+          unpack_chunk<DT, VEC>(v[k], tx[k], a.x_dtype);
+          unpack_chunk<DT, VEC>(t, tr[k], a.residual_dtype);
 #pragma unroll
           for (int i = 0; i < VEC; ++i) v[k][i] += t[i];
         }
       } else {
 #pragma unroll
-        for (int k = 0; k < K; ++k) unpack_chunk<DT, VEC>(v[k], rx[k], a.x_dtype);
+        for (int k = 0; k < K; ++k) unpack_chunk<DT, VEC>(v[k], tx[k], a.x_dtype);
       }
-    }
-    if (a.residual_out != nullptr) {
+      if (a.residual_out != nullptr) {
 #pragma unroll
-      for (int k = 0; k < K; ++k)
-        if (row_ok && cok[k])
-          store_chunk<DT, VEC>(a.residual_out, row * a.residual_out_row_stride + col[k], v[k],
-                               a.residual_out_dtype);
+        for (int k = 0; k < K; ++k)
+          if (row_ok && cok(k))
+            store_chunk<DT, VEC>(a.residual_out, row * a.residual_out_row_stride + col(k), v[k],
+                                 a.residual_out_dtype);
+      }
     }
 
     if (first && p.cluster_n > 1) cluster_wait();
@@ -124,19 +153,37 @@ norm_fwd_kernel(const NormFwdParams p) {
     if constexpr (LN) {
       float s = 0.0f;
 #pragma unroll
-      for (int k = 0; k < K; ++k)
+      for (int k = 0; k < K; ++k) {
+        if constexpr (RAW) {
+          float t[VEC];
+          unpack_chunk<DT, VEC>(t, rx[k], a.x_dtype);
 #pragma unroll
-        for (int i = 0; i < VEC; ++i) s += v[k][i];
+          for (int i = 0; i < VEC; ++i) s += t[i];
+        } else {
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) s += v[k][i];
+        }
+      }
       mean = row_reduce<SumOp>(make_float2(s, 0.f), g, scratch, 0, parity).x * inv_n;
       float q = 0.0f;
 #pragma unroll
       for (int k = 0; k < K; ++k) {
-        // Lanes outside the row must stay zero after centering or they would add mean^2 each.
-        if (cok[k]) {
+        // Lanes outside the row must stay zero after centring or they would add mean^2 each.
+        if (cok(k)) {
+          if constexpr (RAW) {
+            float t[VEC];
+            unpack_chunk<DT, VEC>(t, rx[k], a.x_dtype);
 #pragma unroll
-          for (int i = 0; i < VEC; ++i) {
-            v[k][i] -= mean;
-            q = fmaf(v[k][i], v[k][i], q);
+            for (int i = 0; i < VEC; ++i) {
+              const float d = t[i] - mean;
+              q = fmaf(d, d, q);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) {
+              v[k][i] -= mean;
+              q = fmaf(v[k][i], v[k][i], q);
+            }
           }
         }
       }
@@ -145,9 +192,17 @@ norm_fwd_kernel(const NormFwdParams p) {
     } else {
       float q = 0.0f;
 #pragma unroll
-      for (int k = 0; k < K; ++k)
+      for (int k = 0; k < K; ++k) {
+        if constexpr (RAW) {
+          float t[VEC];
+          unpack_chunk<DT, VEC>(t, rx[k], a.x_dtype);
 #pragma unroll
-        for (int i = 0; i < VEC; ++i) q = fmaf(v[k][i], v[k][i], q);
+          for (int i = 0; i < VEC; ++i) q = fmaf(t[i], t[i], q);
+        } else {
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) q = fmaf(v[k][i], v[k][i], q);
+        }
+      }
       const float ms = row_reduce<SumOp>(make_float2(q, 0.f), g, scratch, 0, parity).x * inv_n;
       rstd = rsqrtf(ms + a.eps);
     }
@@ -161,13 +216,12 @@ norm_fwd_kernel(const NormFwdParams p) {
     // ---- normalise and store ----
 #pragma unroll
     for (int k = 0; k < K; ++k) {
-      float w[VEC], b[VEC];
-      if constexpr (kHoistW) {
-#pragma unroll
-        for (int i = 0; i < VEC; ++i) { w[i] = wr[k][i]; b[i] = br[k][i]; }
-      } else {
+      if (row_ok && cok(k)) {
+        float w[VEC], b[VEC], y[VEC], xc[VEC];
         if (has_w) {
-          load_chunk<kDynDT, VEC, false>(w, a.weight, wrow + col[k], a.weight_dtype, cok[k]);
+          load_chunk_smem<kDynDT, VEC>(
+              w, w_smem + (static_cast<size_t>(k) * nthreads + threadIdx.x) * p.w_slot,
+              a.weight_dtype);
 #pragma unroll
           for (int i = 0; i < VEC; ++i) w[i] += a.weight_offset;
         } else {
@@ -175,45 +229,62 @@ norm_fwd_kernel(const NormFwdParams p) {
           for (int i = 0; i < VEC; ++i) w[i] = 1.0f;
         }
         if (has_b) {
-          load_chunk<kDynDT, VEC, false>(b, a.bias, wrow + col[k], a.bias_dtype, cok[k]);
+          load_chunk_smem<kDynDT, VEC>(
+              b, b_smem + (static_cast<size_t>(k) * nthreads + threadIdx.x) * p.b_slot,
+              a.bias_dtype);
         } else {
 #pragma unroll
           for (int i = 0; i < VEC; ++i) b[i] = 0.0f;
         }
-      }
-      float y[VEC];
+        if constexpr (RAW) {
+          unpack_chunk<DT, VEC>(xc, rx[k], a.x_dtype);
+          if (a.residual_out != nullptr)  // dtype-preserving copy of x (no residual was added)
+            store_chunk<DT, VEC>(a.residual_out, row * a.residual_out_row_stride + col(k), xc,
+                                 a.residual_out_dtype);
+          if constexpr (LN) {
 #pragma unroll
-      for (int i = 0; i < VEC; ++i) y[i] = fmaf(v[k][i] * rstd, w[i], b[i]);
-      if (row_ok && cok[k])
-        store_chunk<DT, VEC>(a.out, row * a.out_row_stride + col[k], y, a.out_dtype);
+            for (int i = 0; i < VEC; ++i) xc[i] -= mean;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) xc[i] = v[k][i];
+        }
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) y[i] = fmaf(xc[i] * rstd, w[i], b[i]);
+        store_chunk<DT, VEC>(a.out, row * a.out_row_stride + col(k), y, a.out_dtype);
+      }
     }
   }
   // A CTA that never entered the loop still owes the wait matching its arrive.
   if (first && p.cluster_n > 1) cluster_wait();
+#undef col
+#undef cok
 }
 
 // ---------------------------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------------------------
-template <int DT, int VEC, int K>
-static int launch_norm_fwd_k(const NormFwdParams& p, dim3 grid, int threads, cudaStream_t st) {
+template <int DT, int VEC, int K, bool RAW>
+static int launch_norm_fwd_k(const NormFwdParams& p, dim3 grid, int threads, size_t smem,
+                             cudaStream_t st) {
   if (p.a.is_layernorm)
-    return launch_kernel(norm_fwd_kernel<DT, VEC, K, true>, grid, threads, 0, p.cluster_n, st, p,
-                         "layernorm_fwd");
-  return launch_kernel(norm_fwd_kernel<DT, VEC, K, false>, grid, threads, 0, p.cluster_n, st, p,
-                       "rmsnorm_fwd");
+    return launch_kernel(norm_fwd_kernel<DT, VEC, K, true, RAW>, grid, threads, smem, p.cluster_n,
+                         st, p, "layernorm_fwd");
+  return launch_kernel(norm_fwd_kernel<DT, VEC, K, false, RAW>, grid, threads, smem, p.cluster_n,
+                       st, p, "rmsnorm_fwd");
 }
 
-template <int DT, int VEC>
-static int launch_norm_fwd_v(const NormFwdParams& p, int K, dim3 grid, int threads,
+template <int DT, int VEC, bool RAW>
+static int launch_norm_fwd_v(const NormFwdParams& p, int K, dim3 grid, int threads, size_t smem,
                              cudaStream_t st) {
   switch (K) {
-    case 1: return launch_norm_fwd_k<DT, VEC, 1>(p, grid, threads, st);
-    case 2: return launch_norm_fwd_k<DT, VEC, 2>(p, grid, threads, st);
-    case 4: return launch_norm_fwd_k<DT, VEC, 4>(p, grid, threads, st);
-    case 8: return launch_norm_fwd_k<DT, VEC, 8>(p, grid, threads, st);
+    case 1: return launch_norm_fwd_k<DT, VEC, 1, RAW>(p, grid, threads, smem, st);
+    case 2: return launch_norm_fwd_k<DT, VEC, 2, RAW>(p, grid, threads, smem, st);
+    case 4: return launch_norm_fwd_k<DT, VEC, 4, RAW>(p, grid, threads, smem, st);
+    case 8: return launch_norm_fwd_k<DT, VEC, 8, RAW>(p, grid, threads, smem, st);
     case 16:
-      if constexpr (VEC <= 4) return launch_norm_fwd_k<DT, VEC, 16>(p, grid, threads, st);
+      if constexpr (VEC <= 4 || RAW)
+        return launch_norm_fwd_k<DT, VEC, 16, RAW>(p, grid, threads, smem, st);
   }
   return set_error(QB_ERR_UNSUPPORTED, "norm_fwd: no kernel for %d chunks of %d per thread", K, VEC);
 }
@@ -257,14 +328,17 @@ extern "C" int qb_norm_fwd(const qb_norm_fwd_args* args, qb_stream_t stream) {
   bool uniform = a.out_dtype == a.x_dtype && (!a.residual || a.residual_dtype == a.x_dtype) &&
                  (!a.residual_out || a.residual_out_dtype == a.x_dtype);
   if (vec != 16 / host_dtype_bytes(a.x_dtype)) uniform = false;
+  // Packed-register mode: 16-bit rows without a residual.
+  const bool raw = uniform && a.residual == nullptr && a.x_dtype != QB_F32;
 
-  // The kernel holds the row as fp32 registers: up to 64 values per thread in CTAs of <= 512
-  // threads (32 on the generic mixed-dtype path, whose raw staging registers are wider) and 16
-  // in CTAs of 1024 threads.
+  // Per-thread capacity in row elements: fp32-held rows 64 (<= 512 threads) / 16 (1024 threads);
+  // packed 16-bit rows twice that; the generic mixed-dtype path (wider staging registers) 32.
   RowPlan plan;
-  const ElemCaps caps = {uniform ? 64 : 32, uniform ? 64 : 32, 16};
-  const int64_t pref = (uniform && vec == 8) ? 16384 : 8192;
-  if (int rc = plan_rows("norm_fwd", a.N, vec, caps, pref, 4, 256, a.cfg, &plan)) return rc;
+  const ElemCaps caps = raw ? ElemCaps{128, 64, 32, 16}
+                            : (uniform ? ElemCaps{64, 64, 16} : ElemCaps{32, 32, 16});
+  const int64_t pref = raw ? 32768 : ((uniform && vec == 8) ? 16384 : 8192);
+  if (int rc = plan_rows("norm_fwd", a.N, vec, caps, pref, raw ? 16 : 8, 128, a.cfg, &plan))
+    return rc;
   const int K = plan.K;
   const int threads = plan.threads;
 
@@ -275,9 +349,21 @@ extern "C" int qb_norm_fwd(const qb_norm_fwd_args* args, qb_stream_t stream) {
   p.cluster_n = plan.cluster_n;
   p.cols_per_cta = plan.cols_per_cta;
   p.num_tiles = ceil_div(a.M, p.rows_per_cta);
-  const int64_t max_ctas = a.cfg.max_ctas > 0
-                               ? a.cfg.max_ctas
-                               : (int64_t)dev->sm_count * (2048 / threads) * 2;
+  p.w_slot = a.weight ? vec * host_dtype_bytes(a.weight_dtype) : 0;
+  p.b_slot = a.bias ? vec * host_dtype_bytes(a.bias_dtype) : 0;
+  const size_t smem = static_cast<size_t>(K) * threads * (p.w_slot + p.b_slot);
+  if (smem + 4096 > static_cast<size_t>(dev->max_smem_optin))
+    return set_error(QB_ERR_UNSUPPORTED,
+                     "norm_fwd: parameter staging of %zu bytes exceeds shared memory", smem);
+  // Persistent grid: enough CTAs to fill every SM at the kernel's occupancy, each walking over
+  // row tiles (so weight / bias are staged once per CTA, not once per row).
+  int per_sm = 2048 / threads;
+  if (smem > 0) {
+    const int by_smem = static_cast<int>(static_cast<size_t>(dev->max_smem_optin) / (smem + 2048));
+    if (per_sm > by_smem) per_sm = by_smem;
+  }
+  if (per_sm < 1) per_sm = 1;
+  const int64_t max_ctas = a.cfg.max_ctas > 0 ? a.cfg.max_ctas : (int64_t)dev->sm_count * per_sm;
   int64_t clusters = p.num_tiles;
   if (clusters > max_ctas / plan.cluster_n) clusters = max_ctas / plan.cluster_n;
   if (clusters < 1) clusters = 1;
@@ -285,16 +371,21 @@ extern "C" int qb_norm_fwd(const qb_norm_fwd_args* args, qb_stream_t stream) {
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
 
   if (uniform) {
+    if (raw) {
+      if (a.x_dtype == QB_BF16)
+        return launch_norm_fwd_v<QB_BF16, 8, true>(p, K, grid, threads, smem, st);
+      return launch_norm_fwd_v<QB_F16, 8, true>(p, K, grid, threads, smem, st);
+    }
     switch (a.x_dtype) {
-      case QB_BF16: return launch_norm_fwd_v<QB_BF16, 8>(p, K, grid, threads, st);
-      case QB_F16: return launch_norm_fwd_v<QB_F16, 8>(p, K, grid, threads, st);
-      default: return launch_norm_fwd_v<QB_F32, 4>(p, K, grid, threads, st);
+      case QB_BF16: return launch_norm_fwd_v<QB_BF16, 8, false>(p, K, grid, threads, smem, st);
+      case QB_F16: return launch_norm_fwd_v<QB_F16, 8, false>(p, K, grid, threads, smem, st);
+      default: return launch_norm_fwd_v<QB_F32, 4, false>(p, K, grid, threads, smem, st);
     }
   }
   switch (vec) {
-    case 8: return launch_norm_fwd_v<kDynDT, 8>(p, K, grid, threads, st);
-    case 4: return launch_norm_fwd_v<kDynDT, 4>(p, K, grid, threads, st);
-    case 2: return launch_norm_fwd_v<kDynDT, 2>(p, K, grid, threads, st);
-    default: return launch_norm_fwd_v<kDynDT, 1>(p, K, grid, threads, st);
+    case 8: return launch_norm_fwd_v<kDynDT, 8, false>(p, K, grid, threads, smem, st);
+    case 4: return launch_norm_fwd_v<kDynDT, 4, false>(p, K, grid, threads, smem, st);
+    case 2: return launch_norm_fwd_v<kDynDT, 2, false>(p, K, grid, threads, smem, st);
+    default: return launch_norm_fwd_v<kDynDT, 1, false>(p, K, grid, threads, smem, st);
   }
 }

@@ -22,72 +22,116 @@ struct SoftmaxParams {
   int64_t num_tiles;
 };
 
-template <int DT, int VEC, int K>
-__global__ void __launch_bounds__((K * VEC > 16) ? 512 : 1024)
+// Maximum of the VEC packed 16-bit elements of a raw chunk (exact: the maximum of bf16 / fp16
+// values is one of them), without unpacking every element.
+template <int DT, int VEC>
+__device__ __forceinline__ float packed_max16(const uint32_t* w) {
+  static_assert(VEC >= 2 && (DT == QB_BF16 || DT == QB_F16), "packed 16-bit chunks only");
+  if constexpr (DT == QB_BF16) {
+    __nv_bfloat162 m = *reinterpret_cast<const __nv_bfloat162*>(&w[0]);
+#pragma unroll
+    for (int i = 1; i < VEC / 2; ++i) m = __hmax2(m, *reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+    return fmaxf(__low2float(m), __high2float(m));
+  } else {
+    __half2 m = *reinterpret_cast<const __half2*>(&w[0]);
+#pragma unroll
+    for (int i = 1; i < VEC / 2; ++i) m = __hmax2(m, *reinterpret_cast<const __half2*>(&w[i]));
+    return fmaxf(__low2float(m), __high2float(m));
+  }
+}
+
+// RAW (16-bit inputs): the row stays packed in registers (twice the bytes in flight per register)
+// and is unpacked by each pass; the exponential is then evaluated twice per element (once for the
+// sum, once for the output).  Otherwise the exponentials are kept as fp32 registers.
+template <int DT, int VEC, int K, bool RAW>
+__global__ void __launch_bounds__(RAW ? (K * VEC > 64 ? 256 : (K * VEC > 32 ? 512 : 1024))
+                                      : (K * VEC > 16 ? 512 : 1024))
 softmax_fwd_kernel(const SoftmaxParams p) {
   __shared__ ReduceScratch scratch;
   const RowGeom g = make_geom(p.tpr, p.cluster_n);
   if (p.cluster_n > 1) cluster_arrive();
   const int col0 = static_cast<int>(g.crank) * p.cols_per_cta;
   const int ncols = min(p.cols_per_cta, p.N - col0);
-  int col[K];
-  bool cok[K];
-#pragma unroll
-  for (int k = 0; k < K; ++k) {
-    const int local = (k * p.tpr + g.t) * VEC;
-    cok[k] = local < ncols;
-    col[k] = col0 + local;
-  }
+  const int colbase = col0 + g.t * VEC;
+  const int cstride = p.tpr * VEC;
+  const int nchunks = ncols > 0 ? ncols / VEC : 0;
+  const int nk = nchunks > g.t ? min(K, (nchunks - g.t + p.tpr - 1) / p.tpr) : 0;
   const int64_t tile_stride = gridDim.x / p.cluster_n;
   int parity = 0;
   bool first = true;
   for (int64_t tile = blockIdx.x / p.cluster_n; tile < p.num_tiles; tile += tile_stride) {
     const int64_t row = tile * p.rows_per_cta + g.r;
     const bool row_ok = row < p.M;
-    float v[K][VEC];
-    {
-      uint32_t rx[K][RawWords<DT, VEC>::value];
-#pragma unroll
-      for (int k = 0; k < K; ++k)
-        load_chunk_raw<DT, VEC>(rx[k], p.in0, row * p.ld0 + col[k], p.dt0, row_ok && cok[k]);
-#pragma unroll
-      for (int k = 0; k < K; ++k) unpack_chunk<DT, VEC>(v[k], rx[k], p.dt0);
-    }
-    // Thread-local maximum over the lanes that exist.
-    float m_t = neg_inf();
-#pragma unroll
-    for (int k = 0; k < K; ++k) {
-      if (row_ok && cok[k]) {
-#pragma unroll
-        for (int i = 0; i < VEC; ++i) m_t = fmaxf(m_t, v[k][i]);
-      } else {
-#pragma unroll
-        for (int i = 0; i < VEC; ++i) v[k][i] = neg_inf();
-      }
-    }
-    // e_i = exp(x_i - m_t) as exp2 of one fused multiply-add; one exponential per element.
-    const float nm = (m_t == neg_inf()) ? 0.0f : -m_t * kLog2e;
-    float s_t = 0.0f;
+    const int nkr = row_ok ? nk : 0;  // chunks of this thread that exist in this tile
+    constexpr int kRawWords = RawWords<DT, VEC>::value;
+    uint32_t rx[K][kRawWords];
 #pragma unroll
     for (int k = 0; k < K; ++k)
+      load_chunk_raw<DT, VEC>(rx[k], p.in0, row * p.ld0 + colbase + k * cstride, p.dt0, k < nkr);
+
+    // Thread-local maximum over the chunks that exist.
+    float m_t = neg_inf();
+    float v[RAW ? 1 : K][VEC];
 #pragma unroll
-      for (int i = 0; i < VEC; ++i) {
-        v[k][i] = fast_exp2(fmaf(v[k][i], kLog2e, nm));
-        s_t += v[k][i];
+    for (int k = 0; k < K; ++k) {
+      if constexpr (RAW) {
+        if (k < nkr) m_t = fmaxf(m_t, packed_max16<DT, VEC>(rx[k]));
+      } else {
+        unpack_chunk<DT, VEC>(v[k], rx[k], p.dt0);
+        if (k < nkr) {
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) m_t = fmaxf(m_t, v[k][i]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) v[k][i] = neg_inf();
+        }
       }
+    }
+    // e_i = exp(x_i - m_t) = 2^(x_i * log2e + off.hi) * 2^off.lo
+    const ExpOffset off = exp_offset(m_t);
+    float s_t = 0.0f;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      if constexpr (RAW) {
+        if (k < nkr) {
+          float t[VEC];
+          unpack_chunk<DT, VEC>(t, rx[k], p.dt0);
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) s_t += fast_exp2(fmaf(t[i], kLog2e, off.hi));
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) {
+          v[k][i] = fast_exp2(fmaf(v[k][i], kLog2e, off.hi));
+          s_t += v[k][i];
+        }
+      }
+    }
+    const float corr = fast_exp2(off.lo);
+    s_t *= corr;
     if (first && p.cluster_n > 1) cluster_wait();
     first = false;
     const float2 ms = row_reduce<MaxSumExpOp>(make_float2(m_t, s_t), g, scratch, 0, parity);
     parity ^= 1;
     // y_i = e_i * exp(m_t - m) / s
-    const float scale =
-        (m_t == neg_inf()) ? 0.0f : fast_exp2((m_t - ms.x) * kLog2e) * (1.0f / ms.y);
+    const float scale = (m_t == neg_inf())
+                            ? 0.0f
+                            : corr * fast_exp2((m_t - ms.x) * kLog2e) * (1.0f / ms.y);
 #pragma unroll
     for (int k = 0; k < K; ++k) {
-      float y[VEC];
+      if (k < nkr) {
+        float y[VEC];
+        if constexpr (RAW) {
+          float t[VEC];
+          unpack_chunk<DT, VEC>(t, rx[k], p.dt0);
 #pragma unroll
-      for (int i = 0; i < VEC; ++i) y[i] = v[k][i] * scale;
-      if (row_ok && cok[k]) store_chunk<DT, VEC>(p.out, row * p.ldo + col[k], y, p.dto);
+          for (int i = 0; i < VEC; ++i) y[i] = fast_exp2(fmaf(t[i], kLog2e, off.hi)) * scale;
+        } else {
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) y[i] = v[k][i] * scale;
+        }
+        store_chunk<DT, VEC>(p.out, row * p.ldo + colbase + k * cstride, y, p.dto);
+      }
     }
   }
   if (first && p.cluster_n > 1) cluster_wait();
@@ -103,14 +147,10 @@ softmax_bwd_kernel(const SoftmaxParams p) {
   if (p.cluster_n > 1) cluster_arrive();
   const int col0 = static_cast<int>(g.crank) * p.cols_per_cta;
   const int ncols = min(p.cols_per_cta, p.N - col0);
-  int col[K];
-  bool cok[K];
-#pragma unroll
-  for (int k = 0; k < K; ++k) {
-    const int local = (k * p.tpr + g.t) * VEC;
-    cok[k] = local < ncols;
-    col[k] = col0 + local;
-  }
+  const int colbase = col0 + g.t * VEC;
+  const int cstride = p.tpr * VEC;
+  const int nchunks = ncols > 0 ? ncols / VEC : 0;
+  const int nk = nchunks > g.t ? min(K, (nchunks - g.t + p.tpr - 1) / p.tpr) : 0;
   const int64_t tile_stride = gridDim.x / p.cluster_n;
   int parity = 0;
   bool first = true;
@@ -121,10 +161,10 @@ softmax_bwd_kernel(const SoftmaxParams p) {
     uint32_t ry[K][RawWords<DT, VEC>::value];
 #pragma unroll
     for (int k = 0; k < K; ++k)
-      load_chunk_raw<DT, VEC>(rdy[k], p.in0, row * p.ld0 + col[k], p.dt0, row_ok && cok[k]);
+      load_chunk_raw<DT, VEC>(rdy[k], p.in0, row * p.ld0 + colbase + k * cstride, p.dt0, row_ok && k < nk);
 #pragma unroll
     for (int k = 0; k < K; ++k)
-      load_chunk_raw<DT, VEC>(ry[k], p.in1, row * p.ld1 + col[k], p.dt1, row_ok && cok[k]);
+      load_chunk_raw<DT, VEC>(ry[k], p.in1, row * p.ld1 + colbase + k * cstride, p.dt1, row_ok && k < nk);
     float dot = 0.0f;
 #pragma unroll
     for (int k = 0; k < K; ++k) {
@@ -145,7 +185,7 @@ softmax_bwd_kernel(const SoftmaxParams p) {
       unpack_chunk<DT, VEC>(y, ry[k], p.dt1);
 #pragma unroll
       for (int i = 0; i < VEC; ++i) dx[i] = y[i] * (dy[i] - dot);
-      if (row_ok && cok[k]) store_chunk<DT, VEC>(p.out, row * p.ldo + col[k], dx, p.dto);
+      if (row_ok && k < nk) store_chunk<DT, VEC>(p.out, row * p.ldo + colbase + k * cstride, dx, p.dto);
     }
   }
   if (first && p.cluster_n > 1) cluster_wait();
@@ -154,31 +194,31 @@ softmax_bwd_kernel(const SoftmaxParams p) {
 // ---------------------------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------------------------
-template <int DT, int VEC, bool BWD>
+template <int DT, int VEC, bool BWD, bool RAW>
 static int launch_softmax_v(const SoftmaxParams& p, int K, dim3 grid, int threads,
                             cudaStream_t st) {
   const char* name = BWD ? "softmax_bwd" : "softmax_fwd";
-#define QB_CASE(KK)                                                                             \
-  case KK:                                                                                      \
-    if constexpr (BWD)                                                                          \
-      return launch_kernel(softmax_bwd_kernel<DT, VEC, KK>, grid, threads, 0, p.cluster_n, st,  \
-                           p, name);                                                            \
-    else                                                                                        \
-      return launch_kernel(softmax_fwd_kernel<DT, VEC, KK>, grid, threads, 0, p.cluster_n, st,  \
-                           p, name);
+#define QB_CASE(KK)                                                                              \
+  case KK:                                                                                       \
+    if constexpr (BWD)                                                                           \
+      return launch_kernel(softmax_bwd_kernel<DT, VEC, KK>, grid, threads, 0, p.cluster_n, st,   \
+                           p, name);                                                             \
+    else                                                                                         \
+      return launch_kernel(softmax_fwd_kernel<DT, VEC, KK, RAW>, grid, threads, 0, p.cluster_n,  \
+                           st, p, name);
   switch (K) {
     QB_CASE(1)
     QB_CASE(2)
     QB_CASE(4)
     QB_CASE(8)
     case 16:
-      if constexpr (VEC <= 4) {
+      if constexpr (VEC <= 4 || (RAW && !BWD)) {
         if constexpr (BWD)
           return launch_kernel(softmax_bwd_kernel<DT, VEC, 16>, grid, threads, 0, p.cluster_n, st,
                                p, name);
         else
-          return launch_kernel(softmax_fwd_kernel<DT, VEC, 16>, grid, threads, 0, p.cluster_n, st,
-                               p, name);
+          return launch_kernel(softmax_fwd_kernel<DT, VEC, 16, RAW>, grid, threads, 0,
+                               p.cluster_n, st, p, name);
       }
   }
 #undef QB_CASE
@@ -191,11 +231,15 @@ static int softmax_dispatch(SoftmaxParams& p, bool uniform, int vec, const qb_la
   const DeviceFacts* dev = current_device_facts();
   if (dev == nullptr) return QB_ERR_CUDA;
   RowPlan plan;
-  // fwd holds the row as fp32 (64 per thread up to 512 threads); bwd holds two packed tensors.
-  const ElemCaps caps = {uniform ? 64 : 32, uniform ? 64 : 32, 16};
-  const int64_t pref = (uniform && vec == 8) ? 16384 : 8192;
-  if (int rc = plan_rows(BWD ? "softmax_bwd" : "softmax_fwd", p.N, vec, caps, pref, 4, 256, cfg,
-                         &plan))
+  // Packed 16-bit rows (forward RAW mode, backward always): 128 elements per thread up to 256
+  // threads, 64 up to 512, 32 at 1024; fp32-held rows half of that.
+  const bool raw = uniform && p.dt0 != QB_F32;
+  const bool packed = raw || (BWD && uniform);
+  ElemCaps caps = packed ? ElemCaps{BWD ? 64 : 128, 64, BWD ? 16 : 32, BWD ? 8 : 16}
+                         : (uniform ? ElemCaps{64, 64, 16} : ElemCaps{32, 32, 16});
+  const int64_t pref = packed ? 32768 : ((uniform && vec == 8) ? 16384 : 8192);
+  if (int rc = plan_rows(BWD ? "softmax_bwd" : "softmax_fwd", p.N, vec, caps, pref,
+                         (packed && !BWD) ? 16 : 8, 128, cfg, &plan))
     return rc;
   p.tpr = plan.tpr;
   p.rows_per_cta = plan.rows_per_cta;
@@ -210,16 +254,16 @@ static int softmax_dispatch(SoftmaxParams& p, bool uniform, int vec, const qb_la
   dim3 grid(static_cast<unsigned>(clusters * plan.cluster_n), 1, 1);
   if (uniform) {
     switch (p.dt0) {
-      case QB_BF16: return launch_softmax_v<QB_BF16, 8, BWD>(p, plan.K, grid, plan.threads, st);
-      case QB_F16: return launch_softmax_v<QB_F16, 8, BWD>(p, plan.K, grid, plan.threads, st);
-      default: return launch_softmax_v<QB_F32, 4, BWD>(p, plan.K, grid, plan.threads, st);
+      case QB_BF16: return launch_softmax_v<QB_BF16, 8, BWD, true>(p, plan.K, grid, plan.threads, st);
+      case QB_F16: return launch_softmax_v<QB_F16, 8, BWD, true>(p, plan.K, grid, plan.threads, st);
+      default: return launch_softmax_v<QB_F32, 4, BWD, false>(p, plan.K, grid, plan.threads, st);
     }
   }
   switch (vec) {
-    case 8: return launch_softmax_v<kDynDT, 8, BWD>(p, plan.K, grid, plan.threads, st);
-    case 4: return launch_softmax_v<kDynDT, 4, BWD>(p, plan.K, grid, plan.threads, st);
-    case 2: return launch_softmax_v<kDynDT, 2, BWD>(p, plan.K, grid, plan.threads, st);
-    default: return launch_softmax_v<kDynDT, 1, BWD>(p, plan.K, grid, plan.threads, st);
+    case 8: return launch_softmax_v<kDynDT, 8, BWD, false>(p, plan.K, grid, plan.threads, st);
+    case 4: return launch_softmax_v<kDynDT, 4, BWD, false>(p, plan.K, grid, plan.threads, st);
+    case 2: return launch_softmax_v<kDynDT, 2, BWD, false>(p, plan.K, grid, plan.threads, st);
+    default: return launch_softmax_v<kDynDT, 1, BWD, false>(p, plan.K, grid, plan.threads, st);
   }
 }
 
