@@ -213,6 +213,10 @@ def time_kernel(fn, iters=10, warmup=3):
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
+    # Queue the launches behind ~15 ms of GPU-side sleep: several of these kernels are shorter than
+    # the host-side launch path, and an event pair around a launch on an idle stream would time
+    # the host, not the kernel.
+    torch.cuda._sleep(int(3e7))
     pairs = []
     for _ in range(iters):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

@@ -268,6 +268,16 @@ __device__ __forceinline__ void pack16(uint32_t* w, const float (&v)[VEC], bool 
   }
 }
 
+// Makes the compiler forget what it knows about the raw words of a chunk (no instruction is
+// emitted).  Kernels that keep a row packed and unpack it once per pass call this before each
+// repeated unpack: otherwise common-subexpression elimination keeps the unpacked fp32 values of
+// the first pass alive in registers, which defeats the purpose of keeping the row packed.
+template <int WORDS>
+__device__ __forceinline__ void forget_values(uint32_t (&w)[WORDS]) {
+#pragma unroll
+  for (int i = 0; i < WORDS; ++i) asm volatile("" : "+r"(w[i]));
+}
+
 // Unpack a raw chunk (as loaded from memory) to fp32.  DT is the compile-time dtype or kDynDT,
 // in which case the run-time code dt decides (a kernel-uniform branch).
 template <int DT, int VEC>

@@ -8,9 +8,9 @@
 // What bounds these kernels is the number of bytes a resident thread keeps in flight, so the row
 // is held in as few registers as possible: with a residual the fp32 sum x + residual (both packed
 // inputs are in flight at once), without one the still-packed 16-bit input words, which are
-// unpacked again by each pass over the row.  Weight and bias are copied once per CTA into
-// thread-private shared-memory slots (a thread only reads back what it copied itself, so no
-// barrier is needed) and the CTA then walks over row tiles.
+// unpacked again by each pass over the row.  Weight (+ offset) and bias are converted to fp32 and
+// copied once per CTA into shared memory (indexed by column, shared by all row groups of the
+// CTA, one barrier); the CTA then walks over row tiles.
 #include "common.cuh"
 #include "host_common.h"
 
@@ -23,38 +23,16 @@ struct NormFwdParams {
   int cluster_n;      // CTAs sharing a row
   int cols_per_cta;   // columns owned by one CTA of the cluster (multiple of VEC)
   int64_t num_tiles;  // ceil(M / rows_per_cta)
-  int w_slot;         // bytes of one staged weight chunk (VEC * sizeof(weight dtype)), 0 if none
-  int b_slot;         // same for bias
+  int stage_params;   // weight / bias slices are staged in shared memory
 };
-
-// Copies one parameter chunk (weight or bias) into this thread's shared-memory slot, keeping the
-// parameter's own element width.
-template <int VEC>
-__device__ __forceinline__ void stage_param_chunk(unsigned char* slot, const void* base,
-                                                  int64_t idx, int dt, bool pred) {
-  float v[VEC];
-  load_chunk<kDynDT, VEC, false>(v, base, idx, dt, pred);
-  if (dt == QB_F32) {
-#pragma unroll
-    for (int i = 0; i < VEC; ++i) reinterpret_cast<float*>(slot)[i] = v[i];
-  } else {
-    uint32_t w[(VEC + 1) / 2];
-    pack16<VEC>(w, v, dt == QB_BF16);
-    if constexpr (VEC == 1) {
-      *reinterpret_cast<unsigned short*>(slot) = static_cast<unsigned short>(w[0]);
-    } else {
-#pragma unroll
-      for (int i = 0; i < VEC / 2; ++i) reinterpret_cast<uint32_t*>(slot)[i] = w[i];
-    }
-  }
-}
 
 // DT: dtype shared by x / residual / out / residual_out, or kDynDT (per-tensor run-time dtypes).
 // VEC: elements per chunk; K: chunks per thread; LN: LayerNorm instead of RMSNorm;
 // RAW: keep the packed input words instead of fp32 values (no residual, static 16-bit DT only).
 template <int DT, int VEC, int K, bool LN, bool RAW>
-__global__ void __launch_bounds__(RAW ? (K * VEC > 64 ? 256 : (K * VEC > 32 ? 512 : 1024))
-                                      : (K * VEC > 16 ? 512 : 1024))
+__global__ void __launch_bounds__(RAW ? (K * VEC > 32 ? 256 : (K * VEC > 16 ? 512 : 1024))
+                                      : (K * VEC > 16 ? 512 : 1024),
+                                  (RAW && K * VEC > 32) ? 2 : 1)
 norm_fwd_kernel(const NormFwdParams p) {
   extern __shared__ __align__(16) unsigned char smem_params[];
   __shared__ ReduceScratch scratch;
@@ -78,21 +56,33 @@ norm_fwd_kernel(const NormFwdParams p) {
 #define col(k) (colbase + (k) * cstride)
 #define cok(k) ((k) < nk)
 
-  // Stage weight and bias: slot (k, tid) belongs to this thread.
+  // Stage this CTA's column slice of (weight + weight_offset) and of the bias in shared memory as
+  // fp32, chunk c at slot c, so that the per-row epilogue needs no dtype dispatch and no global
+  // loads.  Slices too large for a useful occupancy are read from global memory (L1/L2) instead.
   const bool has_w = a.weight != nullptr;
   const bool has_b = a.bias != nullptr;
+  const bool staged = p.stage_params != 0;
   const int64_t wrow = static_cast<int64_t>(h) * N;
-  unsigned char* w_smem = smem_params;
-  unsigned char* b_smem = smem_params + static_cast<size_t>(K) * nthreads * p.w_slot;
+  const int slice_chunks = p.cols_per_cta / VEC;
+  float* w_smem = reinterpret_cast<float*>(smem_params);
+  float* b_smem = w_smem + (has_w ? static_cast<size_t>(slice_chunks) * VEC : 0);
+  if (staged && (has_w || has_b)) {
+    for (int c = threadIdx.x; c < nchunks; c += nthreads) {
+      float pv[VEC];
+      if (has_w) {
+        load_chunk<kDynDT, VEC, false>(pv, a.weight, wrow + col0 + c * VEC, a.weight_dtype);
 #pragma unroll
-  for (int k = 0; k < K; ++k) {
-    if (has_w)
-      stage_param_chunk<VEC>(w_smem + (static_cast<size_t>(k) * nthreads + threadIdx.x) * p.w_slot,
-                             a.weight, wrow + col(k), a.weight_dtype, cok(k));
-    if (has_b)
-      stage_param_chunk<VEC>(b_smem + (static_cast<size_t>(k) * nthreads + threadIdx.x) * p.b_slot,
-                             a.bias, wrow + col(k), a.bias_dtype, cok(k));
+        for (int i = 0; i < VEC; ++i) w_smem[c * VEC + i] = pv[i] + a.weight_offset;
+      }
+      if (has_b) {
+        load_chunk<kDynDT, VEC, false>(pv, a.bias, wrow + col0 + c * VEC, a.bias_dtype);
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) b_smem[c * VEC + i] = pv[i];
+      }
+    }
+    __syncthreads();
   }
+  const int chunk0 = g.t;  // chunk k of this thread is slice chunk chunk0 + k * tpr
 
   const int64_t tile_stride = gridDim.x / p.cluster_n;
   int parity = 0;
@@ -172,6 +162,7 @@ norm_fwd_kernel(const NormFwdParams p) {
         if (cok(k)) {
           if constexpr (RAW) {
             float t[VEC];
+            forget_values(rx[k]);
             unpack_chunk<DT, VEC>(t, rx[k], a.x_dtype);
 #pragma unroll
             for (int i = 0; i < VEC; ++i) {
@@ -219,24 +210,26 @@ norm_fwd_kernel(const NormFwdParams p) {
       if (row_ok && cok(k)) {
         float w[VEC], b[VEC], y[VEC], xc[VEC];
         if (has_w) {
-          load_chunk_smem<kDynDT, VEC>(
-              w, w_smem + (static_cast<size_t>(k) * nthreads + threadIdx.x) * p.w_slot,
-              a.weight_dtype);
+          if (staged) {
+            load_chunk_smem<QB_F32, VEC>(w, w_smem + (chunk0 + k * p.tpr) * VEC, QB_F32);
+          } else {
+            load_chunk<kDynDT, VEC, false>(w, a.weight, wrow + col(k), a.weight_dtype);
 #pragma unroll
-          for (int i = 0; i < VEC; ++i) w[i] += a.weight_offset;
+            for (int i = 0; i < VEC; ++i) w[i] += a.weight_offset;
+          }
         } else {
 #pragma unroll
           for (int i = 0; i < VEC; ++i) w[i] = 1.0f;
         }
         if (has_b) {
-          load_chunk_smem<kDynDT, VEC>(
-              b, b_smem + (static_cast<size_t>(k) * nthreads + threadIdx.x) * p.b_slot,
-              a.bias_dtype);
+          if (staged) load_chunk_smem<QB_F32, VEC>(b, b_smem + (chunk0 + k * p.tpr) * VEC, QB_F32);
+          else load_chunk<kDynDT, VEC, false>(b, a.bias, wrow + col(k), a.bias_dtype);
         } else {
 #pragma unroll
           for (int i = 0; i < VEC; ++i) b[i] = 0.0f;
         }
         if constexpr (RAW) {
+          forget_values(rx[k]);
           unpack_chunk<DT, VEC>(xc, rx[k], a.x_dtype);
           if (a.residual_out != nullptr)  // dtype-preserving copy of x (no residual was added)
             store_chunk<DT, VEC>(a.residual_out, row * a.residual_out_row_stride + col(k), xc,
@@ -334,7 +327,7 @@ extern "C" int qb_norm_fwd(const qb_norm_fwd_args* args, qb_stream_t stream) {
   // Per-thread capacity in row elements: fp32-held rows 64 (<= 512 threads) / 16 (1024 threads);
   // packed 16-bit rows twice that; the generic mixed-dtype path (wider staging registers) 32.
   RowPlan plan;
-  const ElemCaps caps = raw ? ElemCaps{128, 64, 32, 16}
+  const ElemCaps caps = raw ? ElemCaps{128, 32, 16, 16}
                             : (uniform ? ElemCaps{64, 64, 16} : ElemCaps{32, 32, 16});
   const int64_t pref = raw ? 32768 : ((uniform && vec == 8) ? 16384 : 8192);
   if (int rc = plan_rows("norm_fwd", a.N, vec, caps, pref, raw ? 16 : 8, 128, a.cfg, &plan))
@@ -349,12 +342,11 @@ extern "C" int qb_norm_fwd(const qb_norm_fwd_args* args, qb_stream_t stream) {
   p.cluster_n = plan.cluster_n;
   p.cols_per_cta = plan.cols_per_cta;
   p.num_tiles = ceil_div(a.M, p.rows_per_cta);
-  p.w_slot = a.weight ? vec * host_dtype_bytes(a.weight_dtype) : 0;
-  p.b_slot = a.bias ? vec * host_dtype_bytes(a.bias_dtype) : 0;
-  const size_t smem = static_cast<size_t>(K) * threads * (p.w_slot + p.b_slot);
-  if (smem + 4096 > static_cast<size_t>(dev->max_smem_optin))
-    return set_error(QB_ERR_UNSUPPORTED,
-                     "norm_fwd: parameter staging of %zu bytes exceeds shared memory", smem);
+  // fp32 (weight + offset) and bias slices of this CTA's columns, if small enough to leave room
+  // for several CTAs per SM.
+  size_t smem = static_cast<size_t>(plan.cols_per_cta) * 4 * ((a.weight ? 1 : 0) + (a.bias ? 1 : 0));
+  p.stage_params = smem > 0 && smem <= 48 * 1024;
+  if (!p.stage_params) smem = 0;
   // Persistent grid: enough CTAs to fill every SM at the kernel's occupancy, each walking over
   // row tiles (so weight / bias are staged once per CTA, not once per row).
   int per_sm = 2048 / threads;

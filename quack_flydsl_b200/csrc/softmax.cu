@@ -123,6 +123,7 @@ softmax_fwd_kernel(const SoftmaxParams p) {
         float y[VEC];
         if constexpr (RAW) {
           float t[VEC];
+          forget_values(rx[k]);
           unpack_chunk<DT, VEC>(t, rx[k], p.dt0);
 #pragma unroll
           for (int i = 0; i < VEC; ++i) y[i] = fast_exp2(fmaf(t[i], kLog2e, off.hi)) * scale;
@@ -181,6 +182,8 @@ softmax_bwd_kernel(const SoftmaxParams p) {
 #pragma unroll
     for (int k = 0; k < K; ++k) {
       float dy[VEC], y[VEC], dx[VEC];
+      forget_values(rdy[k]);
+      forget_values(ry[k]);
       unpack_chunk<DT, VEC>(dy, rdy[k], p.dt0);
       unpack_chunk<DT, VEC>(y, ry[k], p.dt1);
 #pragma unroll
