@@ -50,7 +50,8 @@ typedef struct qb_launch_cfg {
   int32_t cluster_n;       /* CTAs of a thread-block cluster that share one row (1,2,4,8,16) */
   int32_t max_ctas;        /* cap on the grid (persistent kernels); 0 = heuristic */
   int32_t stages;          /* shared-memory prefetch stages (norm backward); 0 = heuristic */
-  int32_t reserved[3];
+  int32_t flags;           /* bit 0: keep rows as fp32 registers even where the packed 16-bit mode applies */
+  int32_t reserved[2];
 } qb_launch_cfg;
 
 /* Device facts the host side needs for workspace sizing. */

@@ -32,7 +32,8 @@ class LaunchCfg(Structure):
         ("cluster_n", c_int32),
         ("max_ctas", c_int32),
         ("stages", c_int32),
-        ("reserved", c_int32 * 3),
+        ("flags", c_int32),
+        ("reserved", c_int32 * 2),
     ]
 
 
@@ -227,18 +228,19 @@ def ptr(t: Optional[torch.Tensor]) -> Optional[int]:
 
 
 def make_cfg(num_threads: int = 0, threads_per_row: int = 0, cluster_n: int = 0,
-             max_ctas: int = 0, stages: int = 0) -> LaunchCfg:
+             max_ctas: int = 0, stages: int = 0, flags: int = 0) -> LaunchCfg:
     cfg = LaunchCfg()
     cfg.num_threads = int(num_threads)
     cfg.threads_per_row = int(threads_per_row)
     cfg.cluster_n = int(cluster_n)
     cfg.max_ctas = int(max_ctas)
     cfg.stages = int(stages)
+    cfg.flags = int(flags)
     return cfg
 
 
 def env_cfg(op: str) -> Optional[LaunchCfg]:
-    """Launch override from QUACK_B200_CFG="op:threads:threads_per_row:cluster:max_ctas:stages;..."
+    """Launch override from QUACK_B200_CFG="op:threads:threads_per_row:cluster:max_ctas:stages:flags;..."
     (used by tuning sweeps; 0 keeps the heuristic for a field)."""
     spec = os.environ.get("QUACK_B200_CFG")
     if not spec:
@@ -246,8 +248,8 @@ def env_cfg(op: str) -> Optional[LaunchCfg]:
     for item in spec.split(";"):
         parts = item.split(":")
         if parts and parts[0] == op:
-            vals = [int(v) if v else 0 for v in parts[1:6]]
-            vals += [0] * (5 - len(vals))
+            vals = [int(v) if v else 0 for v in parts[1:7]]
+            vals += [0] * (6 - len(vals))
             return make_cfg(*vals)
     return None
 

@@ -291,6 +291,104 @@ __device__ __forceinline__ void unpack_chunk(float (&v)[VEC], const uint32_t* w,
   }
 }
 
+#ifndef QB_USE_F32X2
+#define QB_USE_F32X2 1
+#endif
+// Element-wise helpers on VEC-wide register arrays.  Pairs of lanes go through the packed
+// fp32x2 instructions of sm_100 (fma.rn.f32x2 and friends), which halves the issue slots of the
+// arithmetic: at 2-4 bytes of HBM traffic per element these kernels are bound by instruction
+// issue as much as by bandwidth.
+template <int VEC>
+__device__ __forceinline__ void vmul(float (&o)[VEC], const float (&a)[VEC], const float (&b)[VEC]) {
+  if constexpr (VEC >= 2 && QB_USE_F32X2) {
+#pragma unroll
+    for (int i = 0; i < VEC; i += 2) {
+      const float2 r = __fmul2_rn(make_float2(a[i], a[i + 1]), make_float2(b[i], b[i + 1]));
+      o[i] = r.x; o[i + 1] = r.y;
+    }
+  } else {
+    o[0] = a[0] * b[0];
+  }
+}
+// o = a * b + c
+template <int VEC>
+__device__ __forceinline__ void vfma(float (&o)[VEC], const float (&a)[VEC], const float (&b)[VEC],
+                                     const float (&c)[VEC]) {
+  if constexpr (VEC >= 2 && QB_USE_F32X2) {
+#pragma unroll
+    for (int i = 0; i < VEC; i += 2) {
+      const float2 r = __ffma2_rn(make_float2(a[i], a[i + 1]), make_float2(b[i], b[i + 1]),
+                                  make_float2(c[i], c[i + 1]));
+      o[i] = r.x; o[i + 1] = r.y;
+    }
+  } else {
+    o[0] = fmaf(a[0], b[0], c[0]);
+  }
+}
+// o = a * s + c with a scalar s
+template <int VEC>
+__device__ __forceinline__ void vfma_s(float (&o)[VEC], const float (&a)[VEC], float s,
+                                       const float (&c)[VEC]) {
+  if constexpr (VEC >= 2 && QB_USE_F32X2) {
+    const float2 s2 = make_float2(s, s);
+#pragma unroll
+    for (int i = 0; i < VEC; i += 2) {
+      const float2 r = __ffma2_rn(make_float2(a[i], a[i + 1]), s2, make_float2(c[i], c[i + 1]));
+      o[i] = r.x; o[i + 1] = r.y;
+    }
+  } else {
+    o[0] = fmaf(a[0], s, c[0]);
+  }
+}
+// o = a * s + t with scalars s, t
+template <int VEC>
+__device__ __forceinline__ void vfma_ss(float (&o)[VEC], const float (&a)[VEC], float s, float t) {
+  if constexpr (VEC >= 2 && QB_USE_F32X2) {
+    const float2 s2 = make_float2(s, s), t2 = make_float2(t, t);
+#pragma unroll
+    for (int i = 0; i < VEC; i += 2) {
+      const float2 r = __ffma2_rn(make_float2(a[i], a[i + 1]), s2, t2);
+      o[i] = r.x; o[i + 1] = r.y;
+    }
+  } else {
+    o[0] = fmaf(a[0], s, t);
+  }
+}
+template <int VEC>
+__device__ __forceinline__ void vadd(float (&o)[VEC], const float (&a)[VEC], const float (&b)[VEC]) {
+  if constexpr (VEC >= 2 && QB_USE_F32X2) {
+#pragma unroll
+    for (int i = 0; i < VEC; i += 2) {
+      const float2 r = __fadd2_rn(make_float2(a[i], a[i + 1]), make_float2(b[i], b[i + 1]));
+      o[i] = r.x; o[i + 1] = r.y;
+    }
+  } else {
+    o[0] = a[0] + b[0];
+  }
+}
+template <int VEC>
+__device__ __forceinline__ void vadd_s(float (&o)[VEC], const float (&a)[VEC], float s) {
+  if constexpr (VEC >= 2 && QB_USE_F32X2) {
+    const float2 s2 = make_float2(s, s);
+#pragma unroll
+    for (int i = 0; i < VEC; i += 2) {
+      const float2 r = __fadd2_rn(make_float2(a[i], a[i + 1]), s2);
+      o[i] = r.x; o[i + 1] = r.y;
+    }
+  } else {
+    o[0] = a[0] + s;
+  }
+}
+
+// o = a + b elementwise sum of all lanes (horizontal), used at the end of a pass
+template <int VEC>
+__device__ __forceinline__ float hsum(const float (&a)[VEC]) {
+  float s = a[0];
+#pragma unroll
+  for (int i = 1; i < VEC; ++i) s += a[i];
+  return s;
+}
+
 // ---------------------------------------------------------------------------------------------
 // chunk = VEC consecutive elements (<= 16 bytes for the widest tensor of the launch)
 // ---------------------------------------------------------------------------------------------

@@ -64,6 +64,24 @@ norm_fwd_kernel(const NormFwdParams p) {
   const bool staged = p.stage_params != 0;
   const int64_t wrow = static_cast<int64_t>(h) * N;
   const int slice_chunks = p.cols_per_cta / VEC;
+  // Layout of a staged slice: for 8-element chunks two planes of 4 floats per chunk, so that the
+  // 16-byte reads of neighbouring threads are contiguous (no bank conflicts).
+  const int plane = slice_chunks * 4;
+  auto param_index = [&](int c, int i) -> int {
+    if constexpr (VEC == 8) return (i >> 2) * plane + c * 4 + (i & 3);
+    else return c * VEC + i;
+  };
+  auto load_param = [&](float (&o)[VEC], const float* base, int c) {
+    if constexpr (VEC == 8) {
+      uint32_t lo[4], hi[4];
+      lds_raw<16>(lo, base + c * 4);
+      lds_raw<16>(hi, base + plane + c * 4);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) { o[i] = __uint_as_float(lo[i]); o[4 + i] = __uint_as_float(hi[i]); }
+    } else {
+      load_chunk_smem<QB_F32, VEC>(o, base + c * VEC, QB_F32);
+    }
+  };
   float* w_smem = reinterpret_cast<float*>(smem_params);
   float* b_smem = w_smem + (has_w ? static_cast<size_t>(slice_chunks) * VEC : 0);
   if (staged && (has_w || has_b)) {
@@ -72,12 +90,12 @@ norm_fwd_kernel(const NormFwdParams p) {
       if (has_w) {
         load_chunk<kDynDT, VEC, false>(pv, a.weight, wrow + col0 + c * VEC, a.weight_dtype);
 #pragma unroll
-        for (int i = 0; i < VEC; ++i) w_smem[c * VEC + i] = pv[i] + a.weight_offset;
+        for (int i = 0; i < VEC; ++i) w_smem[param_index(c, i)] = pv[i] + a.weight_offset;
       }
       if (has_b) {
         load_chunk<kDynDT, VEC, false>(pv, a.bias, wrow + col0 + c * VEC, a.bias_dtype);
 #pragma unroll
-        for (int i = 0; i < VEC; ++i) b_smem[c * VEC + i] = pv[i];
+        for (int i = 0; i < VEC; ++i) b_smem[param_index(c, i)] = pv[i];
       }
     }
     __syncthreads();
@@ -137,64 +155,60 @@ norm_fwd_kernel(const NormFwdParams p) {
     if (first && p.cluster_n > 1) cluster_wait();
     first = false;
 
-    // ---- statistics ----
+    // ---- statistics (branch-free: chunks that do not exist were loaded as zeros) ----
     float mean = 0.0f;
     float rstd;
     if constexpr (LN) {
-      float s = 0.0f;
+      float sv[VEC];
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) sv[i] = 0.0f;
 #pragma unroll
       for (int k = 0; k < K; ++k) {
         if constexpr (RAW) {
           float t[VEC];
           unpack_chunk<DT, VEC>(t, rx[k], a.x_dtype);
-#pragma unroll
-          for (int i = 0; i < VEC; ++i) s += t[i];
+          vadd<VEC>(sv, sv, t);
         } else {
-#pragma unroll
-          for (int i = 0; i < VEC; ++i) s += v[k][i];
+          vadd<VEC>(sv, sv, v[k]);
         }
       }
-      mean = row_reduce<SumOp>(make_float2(s, 0.f), g, scratch, 0, parity).x * inv_n;
-      float q = 0.0f;
+      mean = row_reduce<SumOp>(make_float2(hsum<VEC>(sv), 0.f), g, scratch, 0, parity).x * inv_n;
+      // sum (x - mean)^2; padding chunks hold zeros and get offset 0 instead of -mean
+      float qv[VEC];
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) qv[i] = 0.0f;
 #pragma unroll
       for (int k = 0; k < K; ++k) {
-        // Lanes outside the row must stay zero after centring or they would add mean^2 each.
-        if (cok(k)) {
-          if constexpr (RAW) {
-            float t[VEC];
-            forget_values(rx[k]);
-            unpack_chunk<DT, VEC>(t, rx[k], a.x_dtype);
-#pragma unroll
-            for (int i = 0; i < VEC; ++i) {
-              const float d = t[i] - mean;
-              q = fmaf(d, d, q);
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < VEC; ++i) {
-              v[k][i] -= mean;
-              q = fmaf(v[k][i], v[k][i], q);
-            }
-          }
+        float d[VEC];
+        const float off = cok(k) ? -mean : 0.0f;
+        if constexpr (RAW) {
+          float t[VEC];
+          forget_values(rx[k]);
+          unpack_chunk<DT, VEC>(t, rx[k], a.x_dtype);
+          vadd_s<VEC>(d, t, off);
+        } else {
+          vadd_s<VEC>(d, v[k], off);
         }
+        vfma<VEC>(qv, d, d, qv);
       }
+      const float q = hsum<VEC>(qv);
       const float var = row_reduce<SumOp>(make_float2(q, 0.f), g, scratch, 1, parity).x * inv_n;
       rstd = rsqrtf(var + a.eps);
     } else {
-      float q = 0.0f;
+      float qv[VEC];
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) qv[i] = 0.0f;
 #pragma unroll
       for (int k = 0; k < K; ++k) {
         if constexpr (RAW) {
           float t[VEC];
           unpack_chunk<DT, VEC>(t, rx[k], a.x_dtype);
-#pragma unroll
-          for (int i = 0; i < VEC; ++i) q = fmaf(t[i], t[i], q);
+          vfma<VEC>(qv, t, t, qv);
         } else {
-#pragma unroll
-          for (int i = 0; i < VEC; ++i) q = fmaf(v[k][i], v[k][i], q);
+          vfma<VEC>(qv, v[k], v[k], qv);
         }
       }
-      const float ms = row_reduce<SumOp>(make_float2(q, 0.f), g, scratch, 0, parity).x * inv_n;
+      const float ms = row_reduce<SumOp>(make_float2(hsum<VEC>(qv), 0.f), g, scratch, 0, parity).x * inv_n;
       rstd = rsqrtf(ms + a.eps);
     }
     parity ^= 1;
@@ -204,25 +218,26 @@ norm_fwd_kernel(const NormFwdParams p) {
       if (LN && a.mean != nullptr) a.mean[row] = mean;
     }
 
-    // ---- normalise and store ----
+    // ---- normalise and store: y = (x * ra + rb) * w + b with ra = rstd, rb = -mean * rstd ----
+    const float ra = rstd;
+    const float rb = -mean * rstd;
 #pragma unroll
     for (int k = 0; k < K; ++k) {
       if (row_ok && cok(k)) {
         float w[VEC], b[VEC], y[VEC], xc[VEC];
         if (has_w) {
           if (staged) {
-            load_chunk_smem<QB_F32, VEC>(w, w_smem + (chunk0 + k * p.tpr) * VEC, QB_F32);
+            load_param(w, w_smem, chunk0 + k * p.tpr);
           } else {
             load_chunk<kDynDT, VEC, false>(w, a.weight, wrow + col(k), a.weight_dtype);
-#pragma unroll
-            for (int i = 0; i < VEC; ++i) w[i] += a.weight_offset;
+            vadd_s<VEC>(w, w, a.weight_offset);
           }
         } else {
 #pragma unroll
           for (int i = 0; i < VEC; ++i) w[i] = 1.0f;
         }
         if (has_b) {
-          if (staged) load_chunk_smem<QB_F32, VEC>(b, b_smem + (chunk0 + k * p.tpr) * VEC, QB_F32);
+          if (staged) load_param(b, b_smem, chunk0 + k * p.tpr);
           else load_chunk<kDynDT, VEC, false>(b, a.bias, wrow + col(k), a.bias_dtype);
         } else {
 #pragma unroll
@@ -234,16 +249,11 @@ norm_fwd_kernel(const NormFwdParams p) {
           if (a.residual_out != nullptr)  // dtype-preserving copy of x (no residual was added)
             store_chunk<DT, VEC>(a.residual_out, row * a.residual_out_row_stride + col(k), xc,
                                  a.residual_out_dtype);
-          if constexpr (LN) {
-#pragma unroll
-            for (int i = 0; i < VEC; ++i) xc[i] -= mean;
-          }
+          vfma_ss<VEC>(xc, xc, ra, rb);
         } else {
-#pragma unroll
-          for (int i = 0; i < VEC; ++i) xc[i] = v[k][i];
+          vfma_ss<VEC>(xc, v[k], ra, rb);
         }
-#pragma unroll
-        for (int i = 0; i < VEC; ++i) y[i] = fmaf(xc[i] * rstd, w[i], b[i]);
+        vfma<VEC>(y, xc, w, b);
         store_chunk<DT, VEC>(a.out, row * a.out_row_stride + col(k), y, a.out_dtype);
       }
     }
@@ -322,7 +332,7 @@ extern "C" int qb_norm_fwd(const qb_norm_fwd_args* args, qb_stream_t stream) {
                  (!a.residual_out || a.residual_out_dtype == a.x_dtype);
   if (vec != 16 / host_dtype_bytes(a.x_dtype)) uniform = false;
   // Packed-register mode: 16-bit rows without a residual.
-  const bool raw = uniform && a.residual == nullptr && a.x_dtype != QB_F32;
+  const bool raw = uniform && a.residual == nullptr && a.x_dtype != QB_F32 && !(a.cfg.flags & 1);
 
   // Per-thread capacity in row elements: fp32-held rows 64 (<= 512 threads) / 16 (1024 threads);
   // packed 16-bit rows twice that; the generic mixed-dtype path (wider staging registers) 32.

@@ -236,7 +236,7 @@ static int softmax_dispatch(SoftmaxParams& p, bool uniform, int vec, const qb_la
   RowPlan plan;
   // Packed 16-bit rows (forward RAW mode, backward always): 128 elements per thread up to 256
   // threads, 64 up to 512, 32 at 1024; fp32-held rows half of that.
-  const bool raw = uniform && p.dt0 != QB_F32;
+  const bool raw = uniform && p.dt0 != QB_F32 && !(cfg.flags & 1);
   const bool packed = raw || (BWD && uniform);
   ElemCaps caps = packed ? ElemCaps{BWD ? 64 : 128, 64, BWD ? 16 : 32, BWD ? 8 : 16}
                          : (uniform ? ElemCaps{64, 64, 16} : ElemCaps{32, 32, 16});
@@ -257,8 +257,12 @@ static int softmax_dispatch(SoftmaxParams& p, bool uniform, int vec, const qb_la
   dim3 grid(static_cast<unsigned>(clusters * plan.cluster_n), 1, 1);
   if (uniform) {
     switch (p.dt0) {
-      case QB_BF16: return launch_softmax_v<QB_BF16, 8, BWD, true>(p, plan.K, grid, plan.threads, st);
-      case QB_F16: return launch_softmax_v<QB_F16, 8, BWD, true>(p, plan.K, grid, plan.threads, st);
+      case QB_BF16:
+        if (raw || BWD) return launch_softmax_v<QB_BF16, 8, BWD, true>(p, plan.K, grid, plan.threads, st);
+        return launch_softmax_v<QB_BF16, 8, BWD, false>(p, plan.K, grid, plan.threads, st);
+      case QB_F16:
+        if (raw || BWD) return launch_softmax_v<QB_F16, 8, BWD, true>(p, plan.K, grid, plan.threads, st);
+        return launch_softmax_v<QB_F16, 8, BWD, false>(p, plan.K, grid, plan.threads, st);
       default: return launch_softmax_v<QB_F32, 4, BWD, false>(p, plan.K, grid, plan.threads, st);
     }
   }
