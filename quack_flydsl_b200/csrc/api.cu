@@ -1,4 +1,5 @@
 // Library-level entry points: error string, device query, ABI self-description.
+#include <map>
 #include <mutex>
 #include <string.h>
 
@@ -53,6 +54,38 @@ static const DeviceFacts* device_facts(int device) {
     g_facts_ready[device] = true;
   }
   return &g_facts[device];
+}
+
+int cached_occupancy(const void* kernel, int threads, size_t smem) {
+  struct Key {
+    const void* k; int t; size_t s; int dev;
+    bool operator<(const Key& o) const {
+      if (k != o.k) return k < o.k;
+      if (t != o.t) return t < o.t;
+      if (s != o.s) return s < o.s;
+      return dev < o.dev;
+    }
+  };
+  static std::map<Key, int> cache;
+  static std::mutex mu;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const Key key{kernel, threads, smem, dev};
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  int occ = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, threads, smem) != cudaSuccess) {
+    cudaGetLastError();
+    occ = 1;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  cache[key] = occ;
+  return occ;
 }
 
 const DeviceFacts* current_device_facts() {

@@ -137,10 +137,13 @@ __global__ void __launch_bounds__(512) ce_bwd_kernel(const CeBwdParams p) {
     const bool row_ok = row < a.M;
     const int nur = row_ok ? nu : 0;
     uint32_t raw[kCeBwdUnroll][RawWords<DT, VEC>::value];
+    const int esz_x = elem_bytes<DT>(a.x_dtype), esz_dx = elem_bytes<DT>(a.dx_dtype);
+    const char* xp = reinterpret_cast<const char*>(a.x) + (row * a.x_row_stride + colbase) * esz_x;
+    char* dxp = reinterpret_cast<char*>(a.dx) + (row * a.dx_row_stride + colbase) * esz_dx;
+    const int step_x = cstride * esz_x, step_dx = cstride * esz_dx;
 #pragma unroll
     for (int u = 0; u < kCeBwdUnroll; ++u)
-      load_chunk_raw<DT, VEC>(raw[u], a.x, row * a.x_row_stride + colbase + u * cstride, a.x_dtype,
-                              u < nur);
+      load_chunk_raw_p<DT, VEC>(raw[u], xp + u * step_x, a.x_dtype, u < nur);
     // Row scalars (the same addresses for every thread of the row group: broadcast loads).
     float gscale = 0.0f;  // dloss * w[target], 0 for ignored rows
     float lse = 0.0f;
@@ -173,7 +176,7 @@ __global__ void __launch_bounds__(512) ce_bwd_kernel(const CeBwdParams p) {
           for (int i = 0; i < VEC; ++i)
             if (rel == static_cast<unsigned>(i)) d[i] -= gscale;
         }
-        store_chunk<DT, VEC>(a.dx, row * a.dx_row_stride + c, d, a.dx_dtype);
+        store_chunk_p<DT, VEC>(dxp + u * step_dx, d, a.dx_dtype);
       }
     }
   }
@@ -328,7 +331,7 @@ extern "C" int qb_ce_fwd(const qb_ce_fwd_args* args, qb_stream_t stream) {
   vw.add_tensor(a.x, a.x_dtype, a.x_row_stride);
   const int vec = vw.vec;
   const bool uniform = vec == 16 / host_dtype_bytes(a.x_dtype);
-  int threads = a.cfg.num_threads > 0 ? a.cfg.num_threads : 256;
+  int threads = a.cfg.num_threads > 0 ? a.cfg.num_threads : 128;
   if (!is_pow2(threads) || threads < 32 || threads > 512)
     return set_error(QB_ERR_INVALID, "ce_fwd: bad num_threads %d", threads);
   const int64_t chunks = a.N / vec;
@@ -362,7 +365,9 @@ extern "C" int qb_ce_fwd(const qb_ce_fwd_args* args, qb_stream_t stream) {
   p.cols_per_cta = static_cast<int>(ceil_div(chunks, cluster_n) * vec);
   p.num_tiles = ceil_div(a.M, p.rows_per_cta);
   const int64_t max_ctas =
-      a.cfg.max_ctas > 0 ? a.cfg.max_ctas : (int64_t)dev->sm_count * (2048 / threads) * 4;
+      a.cfg.max_ctas > 0 ? a.cfg.max_ctas
+                         : (cluster_n == 1 ? (int64_t)0x7fffffff
+                                           : (int64_t)dev->sm_count * (2048 / threads) * 2);
   int64_t clusters = p.num_tiles;
   if (clusters > max_ctas / cluster_n) clusters = max_ctas / cluster_n;
   if (clusters < 1) clusters = 1;

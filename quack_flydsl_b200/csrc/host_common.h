@@ -194,6 +194,17 @@ inline int plan_rows(const char* op, int64_t N, int vec, const ElemCaps& caps,
   return QB_OK;
 }
 
+// Number of CTAs of `kernel` that are resident on the whole device at once (cached per kernel and
+// launch shape).  Persistent kernels use exactly this many CTAs: more would run as a second,
+// partially filled wave.
+int cached_occupancy(const void* kernel, int threads, size_t smem);
+template <class Params>
+int resident_ctas(void (*kernel)(Params), int threads, size_t smem, int sm_count) {
+  int per_sm = cached_occupancy(reinterpret_cast<const void*>(kernel), threads, smem);
+  if (per_sm < 1) per_sm = 1;
+  return per_sm * sm_count;
+}
+
 // Launches `kernel` with an optional cluster dimension along x (grid.x must be a multiple of it).
 template <class Params>
 int launch_kernel(void (*kernel)(Params), dim3 grid, int threads, size_t smem, int cluster_n,
@@ -234,6 +245,23 @@ int launch_kernel(void (*kernel)(Params), dim3 grid, int threads, size_t smem, i
                      name, grid.x, grid.y, threads, cluster_n, smem, cudaGetErrorString(e));
   }
   return QB_OK;
+}
+
+// Launch of a kernel that walks over `num_tiles` row tiles with a grid-stride loop: the grid is
+// min(num_tiles, CTAs resident on the device) clusters (max_ctas > 0 overrides the cap), times
+// grid_y independent slices (heads).
+template <class Params>
+int launch_persistent(void (*kernel)(Params), int64_t num_tiles, int grid_y, int threads,
+                      size_t smem, int cluster_n, int max_ctas, int sm_count, cudaStream_t stream,
+                      const Params& params, const char* name) {
+  int64_t cap = max_ctas > 0 ? max_ctas : resident_ctas(kernel, threads, smem, sm_count);
+  cap /= cluster_n;
+  if (grid_y > 1 && max_ctas <= 0) cap = (cap + grid_y - 1) / grid_y;
+  if (cap < 1) cap = 1;
+  int64_t clusters = num_tiles < cap ? num_tiles : cap;
+  if (clusters < 1) clusters = 1;
+  dim3 grid(static_cast<unsigned>(clusters * cluster_n), static_cast<unsigned>(grid_y), 1);
+  return launch_kernel(kernel, grid, threads, smem, cluster_n, stream, params, name);
 }
 
 }  // namespace qb

@@ -95,30 +95,39 @@ norm_bwd_kernel(const NormBwdParams p) {
       if constexpr (DB) db[k][i] = 0.0f;
     }
 
+  // Byte strides between this thread's chunks, per tensor (32-bit).
+  const int esz_x = elem_bytes<DT>(a.x_dtype), esz_dy = elem_bytes<DT>(a.dout_dtype),
+            esz_dro = elem_bytes<DT>(a.dresidual_out_dtype), esz_dx = elem_bytes<DT>(a.dx_dtype),
+            esz_dr = elem_bytes<DT>(a.dresidual_dtype);
+  const int step_x = cstride * esz_x, step_dy = cstride * esz_dy, step_dro = cstride * esz_dro,
+            step_dx = cstride * esz_dx, step_dr = cstride * esz_dr;
+
   // Shared-memory ring: stage s, input j, chunk k, thread tid -> one slot of kSlot bytes.
   const int64_t P = gridDim.x / p.cluster_n;
   const int64_t pidx = blockIdx.x / p.cluster_n;
-  const size_t stage_bytes = static_cast<size_t>(p.n_in) * K * nthreads * kSlot;
-  const size_t in_bytes = static_cast<size_t>(K) * nthreads * kSlot;  // one input of one stage
-  unsigned char* const my_slot0 = smem_raw + static_cast<size_t>(threadIdx.x) * kSlot;
-  auto slot_ptr = [&](int stage, int j, int k) -> unsigned char* {
-    return my_slot0 + stage * stage_bytes + j * in_bytes + static_cast<size_t>(k) * nthreads * kSlot;
-  };
+  const int chunk_bytes = nthreads * kSlot;           // between chunks k and k + 1
+  const int in_bytes = K * chunk_bytes;               // one input of one stage
+  const int stage_bytes = p.n_in * in_bytes;          // one stage
+  unsigned char* const my_slot0 = smem_raw + threadIdx.x * kSlot;
   auto issue_tile = [&](int64_t tile, int stage) {
     if (tile < p.num_tiles) {
       const int64_t m = tile * p.rows_per_cta + g.r;
       if (m < a.M) {
         const int64_t row = m * a.H + h;
+        unsigned char* sx = my_slot0 + stage * stage_bytes;
+        const char* xp = reinterpret_cast<const char*>(a.x) + (row * a.x_row_stride + colbase) * esz_x;
+        const char* dp = reinterpret_cast<const char*>(a.dout) + (row * a.dout_row_stride + colbase) * esz_dy;
+        const char* rp = has_dres_out ? reinterpret_cast<const char*>(a.dresidual_out) +
+                                            (row * a.dresidual_out_row_stride + colbase) * esz_dro
+                                      : nullptr;
 #pragma unroll
         for (int k = 0; k < K; ++k) {
           if (k < nk) {
-            const int c = colbase + k * cstride;
-            stage_chunk<DT, VEC>(slot_ptr(stage, 0, k), a.x, row * a.x_row_stride + c, a.x_dtype);
-            stage_chunk<DT, VEC>(slot_ptr(stage, 1, k), a.dout, row * a.dout_row_stride + c,
-                                 a.dout_dtype);
+            stage_chunk_p<DT, VEC>(sx + k * chunk_bytes, xp + k * step_x, a.x_dtype);
+            stage_chunk_p<DT, VEC>(sx + in_bytes + k * chunk_bytes, dp + k * step_dy, a.dout_dtype);
             if (has_dres_out)
-              stage_chunk<DT, VEC>(slot_ptr(stage, 2, k), a.dresidual_out,
-                                   row * a.dresidual_out_row_stride + c, a.dresidual_out_dtype);
+              stage_chunk_p<DT, VEC>(sx + 2 * in_bytes + k * chunk_bytes, rp + k * step_dro,
+                                     a.dresidual_out_dtype);
           }
         }
       }
@@ -148,6 +157,8 @@ norm_bwd_kernel(const NormBwdParams p) {
     const int64_t m = tile * p.rows_per_cta + g.r;
     const int nkr = m < a.M ? nk : 0;  // chunks of this thread that exist in this tile
     const int64_t row = m * a.H + h;
+    const unsigned char* sx = my_slot0 + stage * stage_bytes;  // x slots; dout at + in_bytes
+    char* dxp = reinterpret_cast<char*>(a.dx) + (row * a.dx_row_stride + colbase) * esz_dx;
     const float rstd = rstd_nx;
     const float neg_mean = -mean_nx;
     {
@@ -167,8 +178,8 @@ norm_bwd_kernel(const NormBwdParams p) {
     for (int k = 0; k < K; ++k) {
       if (k < nkr) {
         float x[VEC], dy[VEC], t[VEC];
-        load_chunk_smem<DT, VEC>(x, slot_ptr(stage, 0, k), a.x_dtype);
-        load_chunk_smem<DT, VEC>(dy, slot_ptr(stage, 1, k), a.dout_dtype);
+        load_chunk_smem<DT, VEC>(x, sx + k * chunk_bytes, a.x_dtype);
+        load_chunk_smem<DT, VEC>(dy, sx + in_bytes + k * chunk_bytes, a.dout_dtype);
         if constexpr (LN) vadd_s<VEC>(x, x, neg_mean);
         vmul<VEC>(t, dy, w[k]);
         vfma<VEC>(s1v, x, t, s1v);
@@ -190,10 +201,9 @@ norm_bwd_kernel(const NormBwdParams p) {
 #pragma unroll
     for (int k = 0; k < K; ++k) {
       if (k < nkr) {
-        const int c = colbase + k * cstride;
         float x[VEC], dy[VEC], t[VEC], dx[VEC];
-        load_chunk_smem<DT, VEC>(x, slot_ptr(stage, 0, k), a.x_dtype);
-        load_chunk_smem<DT, VEC>(dy, slot_ptr(stage, 1, k), a.dout_dtype);
+        load_chunk_smem<DT, VEC>(x, sx + k * chunk_bytes, a.x_dtype);
+        load_chunk_smem<DT, VEC>(dy, sx + in_bytes + k * chunk_bytes, a.dout_dtype);
         if constexpr (LN) vadd_s<VEC>(x, x, neg_mean);
         vmul<VEC>(t, dy, w[k]);
         vfma_ss<VEC>(dx, t, ca, cc);      // t * a + c
@@ -203,13 +213,14 @@ norm_bwd_kernel(const NormBwdParams p) {
         if constexpr (DB) vadd<VEC>(db[k], db[k], dy);
         if (has_dres_out) {
           float dr[VEC];
-          load_chunk_smem<DT, VEC>(dr, slot_ptr(stage, 2, k), a.dresidual_out_dtype);
+          load_chunk_smem<DT, VEC>(dr, sx + 2 * in_bytes + k * chunk_bytes, a.dresidual_out_dtype);
           vadd<VEC>(dx, dx, dr);
         }
-        store_chunk<DT, VEC>(a.dx, row * a.dx_row_stride + c, dx, a.dx_dtype);
+        store_chunk_p<DT, VEC>(dxp + k * step_dx, dx, a.dx_dtype);
         if (a.dresidual != nullptr)
-          store_chunk<DT, VEC>(a.dresidual, row * a.dresidual_row_stride + c, dx,
-                               a.dresidual_dtype);
+          store_chunk_p<DT, VEC>(reinterpret_cast<char*>(a.dresidual) +
+                                     (row * a.dresidual_row_stride + colbase) * esz_dr + k * step_dr,
+                                 dx, a.dresidual_dtype);
       }
     }
   }

@@ -29,9 +29,9 @@ struct NormFwdParams {
 // DT: dtype shared by x / residual / out / residual_out, or kDynDT (per-tensor run-time dtypes).
 // VEC: elements per chunk; K: chunks per thread; LN: LayerNorm instead of RMSNorm;
 // RAW: keep the packed input words instead of fp32 values (no residual, static 16-bit DT only).
-template <int DT, int VEC, int K, bool LN, bool RAW>
+template <int DT, int VEC, int K, bool LN, bool RAW, bool STAGED>
 __global__ void __launch_bounds__(RAW ? (K * VEC > 32 ? 256 : (K * VEC > 16 ? 512 : 1024))
-                                      : (K * VEC > 16 ? 512 : 1024),
+                                      : (K * VEC > 32 ? 256 : (K * VEC > 16 ? 512 : 1024)),
                                   (RAW && K * VEC > 32) ? 2 : 1)
 norm_fwd_kernel(const NormFwdParams p) {
   extern __shared__ __align__(16) unsigned char smem_params[];
@@ -47,23 +47,31 @@ norm_fwd_kernel(const NormFwdParams p) {
   const int ncols = min(p.cols_per_cta, N - col0);  // columns this CTA owns (may be <= 0)
   const float inv_n = 1.0f / static_cast<float>(N);
 
-  // Chunk k of this thread starts at column colbase + k * cstride and exists iff k < nk (kept as
-  // two scalars instead of per-chunk arrays to save registers).
+  // Chunk k of this thread starts at column colbase + k * cstride and exists iff k < nk.
   const int colbase = col0 + g.t * VEC;
   const int cstride = p.tpr * VEC;
   const int nchunks = ncols > 0 ? ncols / VEC : 0;
   const int nk = nchunks > g.t ? min(K, (nchunks - g.t + p.tpr - 1) / p.tpr) : 0;
-#define col(k) (colbase + (k) * cstride)
-#define cok(k) ((k) < nk)
+
+  // Byte strides between this thread's chunks, per tensor (32-bit).
+  const int esz_x = elem_bytes<DT>(a.x_dtype);
+  const int esz_r = elem_bytes<DT>(a.residual_dtype);
+  const int esz_o = elem_bytes<DT>(a.out_dtype);
+  const int esz_ro = elem_bytes<DT>(a.residual_out_dtype);
+  const int step_x = cstride * esz_x, step_r = cstride * esz_r, step_o = cstride * esz_o,
+            step_ro = cstride * esz_ro;
 
   // Stage this CTA's column slice of (weight + weight_offset) and of the bias in shared memory as
-  // fp32, chunk c at slot c, so that the per-row epilogue needs no dtype dispatch and no global
-  // loads.  Slices too large for a useful occupancy are read from global memory (L1/L2) instead.
+  // fp32 (ones / zeros when absent), chunk c at slot c, so that the per-row epilogue needs no
+  // dtype dispatch, no presence checks and no global loads.  Slices too large for a useful
+  // occupancy are read from global memory (L1/L2) instead.
   const bool has_w = a.weight != nullptr;
   const bool has_b = a.bias != nullptr;
-  const bool staged = p.stage_params != 0;
+  constexpr bool staged = STAGED;
   const int64_t wrow = static_cast<int64_t>(h) * N;
-  const int slice_chunks = p.cols_per_cta / VEC;
+  // Slots exist for all tpr * K chunk positions of the tile geometry (the epilogue reads the
+  // slots of padding chunks too, it only does not store their results).
+  const int slice_chunks = p.tpr * K;
   // Layout of a staged slice: for 8-element chunks two planes of 4 floats per chunk, so that the
   // 16-byte reads of neighbouring threads are contiguous (no bank conflicts).
   const int plane = slice_chunks * 4;
@@ -83,20 +91,17 @@ norm_fwd_kernel(const NormFwdParams p) {
     }
   };
   float* w_smem = reinterpret_cast<float*>(smem_params);
-  float* b_smem = w_smem + (has_w ? static_cast<size_t>(slice_chunks) * VEC : 0);
-  if (staged && (has_w || has_b)) {
+  float* b_smem = w_smem + static_cast<size_t>(slice_chunks) * VEC;
+  if constexpr (staged) {
     for (int c = threadIdx.x; c < nchunks; c += nthreads) {
       float pv[VEC];
-      if (has_w) {
-        load_chunk<kDynDT, VEC, false>(pv, a.weight, wrow + col0 + c * VEC, a.weight_dtype);
+      if (has_w) load_chunk<kDynDT, VEC, false>(pv, a.weight, wrow + col0 + c * VEC, a.weight_dtype);
 #pragma unroll
-        for (int i = 0; i < VEC; ++i) w_smem[param_index(c, i)] = pv[i] + a.weight_offset;
-      }
-      if (has_b) {
-        load_chunk<kDynDT, VEC, false>(pv, a.bias, wrow + col0 + c * VEC, a.bias_dtype);
+      for (int i = 0; i < VEC; ++i)
+        w_smem[param_index(c, i)] = has_w ? pv[i] + a.weight_offset : 1.0f;
+      if (has_b) load_chunk<kDynDT, VEC, false>(pv, a.bias, wrow + col0 + c * VEC, a.bias_dtype);
 #pragma unroll
-        for (int i = 0; i < VEC; ++i) b_smem[param_index(c, i)] = pv[i];
-      }
+      for (int i = 0; i < VEC; ++i) b_smem[param_index(c, i)] = has_b ? pv[i] : 0.0f;
     }
     __syncthreads();
   }
@@ -109,6 +114,9 @@ norm_fwd_kernel(const NormFwdParams p) {
     const int64_t m = tile * p.rows_per_cta + g.r;
     const bool row_ok = m < a.M;
     const int64_t row = m * a.H + h;
+    const int nkr = row_ok ? nk : 0;  // chunks of this thread that exist in this tile
+    const char* xp = reinterpret_cast<const char*>(a.x) + (row * a.x_row_stride + colbase) * esz_x;
+    char* op = reinterpret_cast<char*>(a.out) + (row * a.out_row_stride + colbase) * esz_o;
 
     // ---- load the row (all loads issued before the first use) ----
     constexpr int kRawWords = RawWords<DT, VEC>::value;
@@ -117,38 +125,36 @@ norm_fwd_kernel(const NormFwdParams p) {
     if constexpr (RAW) {
 #pragma unroll
       for (int k = 0; k < K; ++k)
-        load_chunk_raw<DT, VEC>(rx[k], a.x, row * a.x_row_stride + col(k), a.x_dtype,
-                                row_ok && cok(k));
+        load_chunk_raw_p<DT, VEC>(rx[k], xp + k * step_x, a.x_dtype, k < nkr);
     } else {
       uint32_t tx[K][kRawWords];
 #pragma unroll
       for (int k = 0; k < K; ++k)
-        load_chunk_raw<DT, VEC>(tx[k], a.x, row * a.x_row_stride + col(k), a.x_dtype,
-                                row_ok && cok(k));
+        load_chunk_raw_p<DT, VEC>(tx[k], xp + k * step_x, a.x_dtype, k < nkr);
       if (a.residual != nullptr) {
+        const char* rp = reinterpret_cast<const char*>(a.residual) +
+                         (row * a.residual_row_stride + colbase) * esz_r;
         uint32_t tr[K][kRawWords];
 #pragma unroll
         for (int k = 0; k < K; ++k)
-          load_chunk_raw<DT, VEC>(tr[k], a.residual, row * a.residual_row_stride + col(k),
-                                  a.residual_dtype, row_ok && cok(k));
+          load_chunk_raw_p<DT, VEC>(tr[k], rp + k * step_r, a.residual_dtype, k < nkr);
 #pragma unroll
         for (int k = 0; k < K; ++k) {
           float t[VEC];
           unpack_chunk<DT, VEC>(v[k], tx[k], a.x_dtype);
           unpack_chunk<DT, VEC>(t, tr[k], a.residual_dtype);
-#pragma unroll
-          for (int i = 0; i < VEC; ++i) v[k][i] += t[i];
+          vadd<VEC>(v[k], v[k], t);
         }
       } else {
 #pragma unroll
         for (int k = 0; k < K; ++k) unpack_chunk<DT, VEC>(v[k], tx[k], a.x_dtype);
       }
       if (a.residual_out != nullptr) {
+        char* rop = reinterpret_cast<char*>(a.residual_out) +
+                    (row * a.residual_out_row_stride + colbase) * esz_ro;
 #pragma unroll
         for (int k = 0; k < K; ++k)
-          if (row_ok && cok(k))
-            store_chunk<DT, VEC>(a.residual_out, row * a.residual_out_row_stride + col(k), v[k],
-                                 a.residual_out_dtype);
+          if (k < nkr) store_chunk_p<DT, VEC>(rop + k * step_ro, v[k], a.residual_out_dtype);
       }
     }
 
@@ -180,7 +186,7 @@ norm_fwd_kernel(const NormFwdParams p) {
 #pragma unroll
       for (int k = 0; k < K; ++k) {
         float d[VEC];
-        const float off = cok(k) ? -mean : 0.0f;
+        const float off = (k < nk) ? -mean : 0.0f;
         if constexpr (RAW) {
           float t[VEC];
           forget_values(rx[k]);
@@ -191,8 +197,8 @@ norm_fwd_kernel(const NormFwdParams p) {
         }
         vfma<VEC>(qv, d, d, qv);
       }
-      const float q = hsum<VEC>(qv);
-      const float var = row_reduce<SumOp>(make_float2(q, 0.f), g, scratch, 1, parity).x * inv_n;
+      const float var =
+          row_reduce<SumOp>(make_float2(hsum<VEC>(qv), 0.f), g, scratch, 1, parity).x * inv_n;
       rstd = rsqrtf(var + a.eps);
     } else {
       float qv[VEC];
@@ -208,7 +214,8 @@ norm_fwd_kernel(const NormFwdParams p) {
           vfma<VEC>(qv, v[k], v[k], qv);
         }
       }
-      const float ms = row_reduce<SumOp>(make_float2(hsum<VEC>(qv), 0.f), g, scratch, 0, parity).x * inv_n;
+      const float ms =
+          row_reduce<SumOp>(make_float2(hsum<VEC>(qv), 0.f), g, scratch, 0, parity).x * inv_n;
       rstd = rsqrtf(ms + a.eps);
     }
     parity ^= 1;
@@ -221,64 +228,87 @@ norm_fwd_kernel(const NormFwdParams p) {
     // ---- normalise and store: y = (x * ra + rb) * w + b with ra = rstd, rb = -mean * rstd ----
     const float ra = rstd;
     const float rb = -mean * rstd;
+    if constexpr (staged) {
 #pragma unroll
-    for (int k = 0; k < K; ++k) {
-      if (row_ok && cok(k)) {
+      for (int k = 0; k < K; ++k) {
         float w[VEC], b[VEC], y[VEC], xc[VEC];
-        if (has_w) {
-          if (staged) {
-            load_param(w, w_smem, chunk0 + k * p.tpr);
-          } else {
-            load_chunk<kDynDT, VEC, false>(w, a.weight, wrow + col(k), a.weight_dtype);
-            vadd_s<VEC>(w, w, a.weight_offset);
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < VEC; ++i) w[i] = 1.0f;
-        }
-        if (has_b) {
-          if (staged) load_param(b, b_smem, chunk0 + k * p.tpr);
-          else load_chunk<kDynDT, VEC, false>(b, a.bias, wrow + col(k), a.bias_dtype);
-        } else {
-#pragma unroll
-          for (int i = 0; i < VEC; ++i) b[i] = 0.0f;
-        }
+        load_param(w, w_smem, chunk0 + k * p.tpr);
+        load_param(b, b_smem, chunk0 + k * p.tpr);
         if constexpr (RAW) {
           forget_values(rx[k]);
           unpack_chunk<DT, VEC>(xc, rx[k], a.x_dtype);
-          if (a.residual_out != nullptr)  // dtype-preserving copy of x (no residual was added)
-            store_chunk<DT, VEC>(a.residual_out, row * a.residual_out_row_stride + col(k), xc,
-                                 a.residual_out_dtype);
           vfma_ss<VEC>(xc, xc, ra, rb);
         } else {
           vfma_ss<VEC>(xc, v[k], ra, rb);
         }
         vfma<VEC>(y, xc, w, b);
-        store_chunk<DT, VEC>(a.out, row * a.out_row_stride + col(k), y, a.out_dtype);
+        if (k < nkr) store_chunk_p<DT, VEC>(op + k * step_o, y, a.out_dtype);
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        if (k < nkr) {
+          float w[VEC], b[VEC], y[VEC], xc[VEC];
+          const int c = colbase + k * cstride;
+          if (has_w) {
+            load_chunk<kDynDT, VEC, false>(w, a.weight, wrow + c, a.weight_dtype);
+            vadd_s<VEC>(w, w, a.weight_offset);
+          } else {
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) w[i] = 1.0f;
+          }
+          if (has_b) {
+            load_chunk<kDynDT, VEC, false>(b, a.bias, wrow + c, a.bias_dtype);
+          } else {
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) b[i] = 0.0f;
+          }
+          if constexpr (RAW) {
+            forget_values(rx[k]);
+            unpack_chunk<DT, VEC>(xc, rx[k], a.x_dtype);
+            vfma_ss<VEC>(xc, xc, ra, rb);
+          } else {
+            vfma_ss<VEC>(xc, v[k], ra, rb);
+          }
+          vfma<VEC>(y, xc, w, b);
+          store_chunk_p<DT, VEC>(op + k * step_o, y, a.out_dtype);
+        }
       }
     }
   }
   // A CTA that never entered the loop still owes the wait matching its arrive.
   if (first && p.cluster_n > 1) cluster_wait();
-#undef col
-#undef cok
 }
 
 // ---------------------------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------------------------
-template <int DT, int VEC, int K, bool RAW>
-static int launch_norm_fwd_k(const NormFwdParams& p, dim3 grid, int threads, size_t smem,
+struct FwdGrid {
+  int max_ctas;  // override of the persistent-grid cap (0 = resident CTAs)
+  int sm_count;
+};
+
+template <int DT, int VEC, int K, bool RAW, bool LN>
+static int launch_norm_fwd_s(const NormFwdParams& p, FwdGrid grid, int threads, size_t smem,
                              cudaStream_t st) {
-  if (p.a.is_layernorm)
-    return launch_kernel(norm_fwd_kernel<DT, VEC, K, true, RAW>, grid, threads, smem, p.cluster_n,
-                         st, p, "layernorm_fwd");
-  return launch_kernel(norm_fwd_kernel<DT, VEC, K, false, RAW>, grid, threads, smem, p.cluster_n,
-                       st, p, "rmsnorm_fwd");
+  const int heads = static_cast<int>(p.a.H);
+  const char* name = LN ? "layernorm_fwd" : "rmsnorm_fwd";
+  if (p.stage_params)
+    return launch_persistent(norm_fwd_kernel<DT, VEC, K, LN, RAW, true>, p.num_tiles, heads,
+                             threads, smem, p.cluster_n, grid.max_ctas, grid.sm_count, st, p, name);
+  return launch_persistent(norm_fwd_kernel<DT, VEC, K, LN, RAW, false>, p.num_tiles, heads, threads,
+                           smem, p.cluster_n, grid.max_ctas, grid.sm_count, st, p, name);
+}
+
+template <int DT, int VEC, int K, bool RAW>
+static int launch_norm_fwd_k(const NormFwdParams& p, FwdGrid grid, int threads, size_t smem,
+                             cudaStream_t st) {
+  if (p.a.is_layernorm) return launch_norm_fwd_s<DT, VEC, K, RAW, true>(p, grid, threads, smem, st);
+  return launch_norm_fwd_s<DT, VEC, K, RAW, false>(p, grid, threads, smem, st);
 }
 
 template <int DT, int VEC, bool RAW>
-static int launch_norm_fwd_v(const NormFwdParams& p, int K, dim3 grid, int threads, size_t smem,
+static int launch_norm_fwd_v(const NormFwdParams& p, int K, FwdGrid grid, int threads, size_t smem,
                              cudaStream_t st) {
   switch (K) {
     case 1: return launch_norm_fwd_k<DT, VEC, 1, RAW>(p, grid, threads, smem, st);
@@ -332,13 +362,14 @@ extern "C" int qb_norm_fwd(const qb_norm_fwd_args* args, qb_stream_t stream) {
                  (!a.residual_out || a.residual_out_dtype == a.x_dtype);
   if (vec != 16 / host_dtype_bytes(a.x_dtype)) uniform = false;
   // Packed-register mode: 16-bit rows without a residual.
-  const bool raw = uniform && a.residual == nullptr && a.x_dtype != QB_F32 && !(a.cfg.flags & 1);
+  const bool raw = uniform && a.residual == nullptr && a.residual_out == nullptr &&
+                   a.x_dtype != QB_F32 && !(a.cfg.flags & 1);
 
   // Per-thread capacity in row elements: fp32-held rows 64 (<= 512 threads) / 16 (1024 threads);
   // packed 16-bit rows twice that; the generic mixed-dtype path (wider staging registers) 32.
   RowPlan plan;
   const ElemCaps caps = raw ? ElemCaps{128, 32, 16, 16}
-                            : (uniform ? ElemCaps{64, 64, 16} : ElemCaps{32, 32, 16});
+                            : (uniform ? ElemCaps{64, 32, 16} : ElemCaps{32, 32, 16});
   const int64_t pref = raw ? 32768 : ((uniform && vec == 8) ? 16384 : 8192);
   if (int rc = plan_rows("norm_fwd", a.N, vec, caps, pref, raw ? 16 : 8, 128, a.cfg, &plan))
     return rc;
@@ -352,24 +383,14 @@ extern "C" int qb_norm_fwd(const qb_norm_fwd_args* args, qb_stream_t stream) {
   p.cluster_n = plan.cluster_n;
   p.cols_per_cta = plan.cols_per_cta;
   p.num_tiles = ceil_div(a.M, p.rows_per_cta);
-  // fp32 (weight + offset) and bias slices of this CTA's columns, if small enough to leave room
-  // for several CTAs per SM.
-  size_t smem = static_cast<size_t>(plan.cols_per_cta) * 4 * ((a.weight ? 1 : 0) + (a.bias ? 1 : 0));
-  p.stage_params = smem > 0 && smem <= 48 * 1024;
+  // fp32 (weight + offset) and bias slices of this CTA's columns (ones / zeros when absent), if
+  // small enough to leave room for several CTAs per SM.
+  size_t smem = static_cast<size_t>(plan.tpr) * plan.K * vec * 8;
+  p.stage_params = smem <= 64 * 1024;
   if (!p.stage_params) smem = 0;
-  // Persistent grid: enough CTAs to fill every SM at the kernel's occupancy, each walking over
-  // row tiles (so weight / bias are staged once per CTA, not once per row).
-  int per_sm = 2048 / threads;
-  if (smem > 0) {
-    const int by_smem = static_cast<int>(static_cast<size_t>(dev->max_smem_optin) / (smem + 2048));
-    if (per_sm > by_smem) per_sm = by_smem;
-  }
-  if (per_sm < 1) per_sm = 1;
-  const int64_t max_ctas = a.cfg.max_ctas > 0 ? a.cfg.max_ctas : (int64_t)dev->sm_count * per_sm;
-  int64_t clusters = p.num_tiles;
-  if (clusters > max_ctas / plan.cluster_n) clusters = max_ctas / plan.cluster_n;
-  if (clusters < 1) clusters = 1;
-  dim3 grid(static_cast<unsigned>(clusters * plan.cluster_n), static_cast<unsigned>(a.H), 1);
+  // Persistent grid: exactly the CTAs that are resident at once, each walking over row tiles (so
+  // weight / bias are staged once per CTA, not once per row).
+  const FwdGrid grid = {a.cfg.max_ctas, dev->sm_count};
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
 
   if (uniform) {

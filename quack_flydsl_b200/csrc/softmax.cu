@@ -65,9 +65,13 @@ softmax_fwd_kernel(const SoftmaxParams p) {
     const int nkr = row_ok ? nk : 0;  // chunks of this thread that exist in this tile
     constexpr int kRawWords = RawWords<DT, VEC>::value;
     uint32_t rx[K][kRawWords];
+    const int esz_i = elem_bytes<DT>(p.dt0), esz_o = elem_bytes<DT>(p.dto);
+    const char* xp = reinterpret_cast<const char*>(p.in0) + (row * p.ld0 + colbase) * esz_i;
+    char* op = reinterpret_cast<char*>(p.out) + (row * p.ldo + colbase) * esz_o;
+    const int step_i = cstride * esz_i, step_o = cstride * esz_o;
 #pragma unroll
     for (int k = 0; k < K; ++k)
-      load_chunk_raw<DT, VEC>(rx[k], p.in0, row * p.ld0 + colbase + k * cstride, p.dt0, k < nkr);
+      load_chunk_raw_p<DT, VEC>(rx[k], xp + k * step_i, p.dt0, k < nkr);
 
     // Thread-local maximum over the chunks that exist.
     float m_t = neg_inf();
@@ -131,7 +135,7 @@ softmax_fwd_kernel(const SoftmaxParams p) {
 #pragma unroll
           for (int i = 0; i < VEC; ++i) y[i] = v[k][i] * scale;
         }
-        store_chunk<DT, VEC>(p.out, row * p.ldo + colbase + k * cstride, y, p.dto);
+        store_chunk_p<DT, VEC>(op + k * step_o, y, p.dto);
       }
     }
   }
@@ -160,12 +164,16 @@ softmax_bwd_kernel(const SoftmaxParams p) {
     const bool row_ok = row < p.M;
     uint32_t rdy[K][RawWords<DT, VEC>::value];
     uint32_t ry[K][RawWords<DT, VEC>::value];
+    const int nkr = row_ok ? nk : 0;
+    const int esz0 = elem_bytes<DT>(p.dt0), esz1 = elem_bytes<DT>(p.dt1), esz_o = elem_bytes<DT>(p.dto);
+    const char* dyp = reinterpret_cast<const char*>(p.in0) + (row * p.ld0 + colbase) * esz0;
+    const char* yp = reinterpret_cast<const char*>(p.in1) + (row * p.ld1 + colbase) * esz1;
+    char* op = reinterpret_cast<char*>(p.out) + (row * p.ldo + colbase) * esz_o;
+    const int step0 = cstride * esz0, step1 = cstride * esz1, step_o = cstride * esz_o;
 #pragma unroll
-    for (int k = 0; k < K; ++k)
-      load_chunk_raw<DT, VEC>(rdy[k], p.in0, row * p.ld0 + colbase + k * cstride, p.dt0, row_ok && k < nk);
+    for (int k = 0; k < K; ++k) load_chunk_raw_p<DT, VEC>(rdy[k], dyp + k * step0, p.dt0, k < nkr);
 #pragma unroll
-    for (int k = 0; k < K; ++k)
-      load_chunk_raw<DT, VEC>(ry[k], p.in1, row * p.ld1 + colbase + k * cstride, p.dt1, row_ok && k < nk);
+    for (int k = 0; k < K; ++k) load_chunk_raw_p<DT, VEC>(ry[k], yp + k * step1, p.dt1, k < nkr);
     float dot = 0.0f;
 #pragma unroll
     for (int k = 0; k < K; ++k) {
@@ -188,7 +196,7 @@ softmax_bwd_kernel(const SoftmaxParams p) {
       unpack_chunk<DT, VEC>(y, ry[k], p.dt1);
 #pragma unroll
       for (int i = 0; i < VEC; ++i) dx[i] = y[i] * (dy[i] - dot);
-      if (row_ok && k < nk) store_chunk<DT, VEC>(p.out, row * p.ldo + colbase + k * cstride, dx, p.dto);
+      if (k < nkr) store_chunk_p<DT, VEC>(op + k * step_o, dx, p.dto);
     }
   }
   if (first && p.cluster_n > 1) cluster_wait();
@@ -249,8 +257,13 @@ static int softmax_dispatch(SoftmaxParams& p, bool uniform, int vec, const qb_la
   p.cluster_n = plan.cluster_n;
   p.cols_per_cta = plan.cols_per_cta;
   p.num_tiles = ceil_div(p.M, p.rows_per_cta);
+  // Rows owned by a single CTA: one tile per CTA (nothing to amortise, and the hardware block
+  // scheduler balances best).  Rows split over a cluster: a bounded grid whose clusters walk over
+  // rows, so that the cluster start-up handshake is paid once per CTA.
   const int64_t max_ctas =
-      cfg.max_ctas > 0 ? cfg.max_ctas : (int64_t)dev->sm_count * (2048 / plan.threads) * 2;
+      cfg.max_ctas > 0 ? cfg.max_ctas
+                       : (plan.cluster_n == 1 ? (int64_t)0x7fffffff
+                                              : (int64_t)dev->sm_count * (2048 / plan.threads) * 2);
   int64_t clusters = p.num_tiles;
   if (clusters > max_ctas / plan.cluster_n) clusters = max_ctas / plan.cluster_n;
   if (clusters < 1) clusters = 1;
