@@ -76,7 +76,7 @@ int cached_occupancy(const void* kernel, int threads, size_t smem) {
     auto it = cache.find(key);
     if (it != cache.end()) return it->second;
   }
-  if (smem > 48 * 1024)
+  if (smem > 32 * 1024)
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   int occ = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, threads, smem) != cudaSuccess) {

@@ -209,7 +209,7 @@ int resident_ctas(void (*kernel)(Params), int threads, size_t smem, int sm_count
 template <class Params>
 int launch_kernel(void (*kernel)(Params), dim3 grid, int threads, size_t smem, int cluster_n,
                   cudaStream_t stream, const Params& params, const char* name) {
-  if (smem > 48 * 1024) {
+  if (smem > 32 * 1024) {  // static + dynamic shared memory above 48 KB needs the opt-in
     cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(kernel),
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) {

@@ -8,6 +8,8 @@
 // through a multi-stage ring; every thread reads back only the bytes it copied itself, so the
 // ring needs no barriers.  Stage 2 replaces the reference's `dw_partial.sum(dim=0)`
 // (quack/rmsnorm.py:1398-1399) by a fixed-order tree, so dw / db are bit-reproducible.
+#include <type_traits>
+
 #include "common.cuh"
 #include "host_common.h"
 
@@ -170,25 +172,34 @@ norm_bwd_kernel(const NormBwdParams p) {
     }
     cp_async_wait_dyn(S - 1);  // this tile's group has landed; S-1 younger groups may be in flight
 
+    // Both passes exist in two forms: FULL (every chunk of this thread exists and there is no
+    // residual-gradient stream: straight-line code, no per-chunk branches) and the general form.
+    // The row reduction between the passes stays outside of the per-thread choice, because it
+    // contains a barrier.
+    const bool full = (nkr == K) && !has_dres_out && a.dresidual == nullptr;
+
     // ---- pass 1: S1 = sum(xc * t), S2 = sum(t) ----
     float s1v[VEC], s2v[VEC];
 #pragma unroll
     for (int i = 0; i < VEC; ++i) { s1v[i] = 0.0f; s2v[i] = 0.0f; }
+    auto pass1 = [&](auto full_tag) {
+      constexpr bool FULL = decltype(full_tag)::value;
 #pragma unroll
-    for (int k = 0; k < K; ++k) {
-      if (k < nkr) {
-        float x[VEC], dy[VEC], t[VEC];
-        load_chunk_smem<DT, VEC>(x, sx + k * chunk_bytes, a.x_dtype);
-        load_chunk_smem<DT, VEC>(dy, sx + in_bytes + k * chunk_bytes, a.dout_dtype);
-        if constexpr (LN) vadd_s<VEC>(x, x, neg_mean);
-        vmul<VEC>(t, dy, w[k]);
-        vfma<VEC>(s1v, x, t, s1v);
-        if constexpr (LN) vadd<VEC>(s2v, s2v, t);
+      for (int k = 0; k < K; ++k) {
+        if (FULL || k < nkr) {
+          float x[VEC], dy[VEC], t[VEC];
+          load_chunk_smem<DT, VEC>(x, sx + k * chunk_bytes, a.x_dtype);
+          load_chunk_smem<DT, VEC>(dy, sx + in_bytes + k * chunk_bytes, a.dout_dtype);
+          if constexpr (LN) vadd_s<VEC>(x, x, neg_mean);
+          vmul<VEC>(t, dy, w[k]);
+          vfma<VEC>(s1v, x, t, s1v);
+          if constexpr (LN) vadd<VEC>(s2v, s2v, t);
+        }
       }
-    }
-    float s1 = 0.0f, s2 = 0.0f;
-#pragma unroll
-    for (int i = 0; i < VEC; ++i) { s1 += s1v[i]; s2 += s2v[i]; }
+    };
+    if (full) pass1(std::true_type{}); else pass1(std::false_type{});
+    const float s1 = hsum<VEC>(s1v);
+    const float s2 = LN ? hsum<VEC>(s2v) : 0.0f;
     if (first && p.cluster_n > 1) cluster_wait();
     first = false;
     const float2 red = row_reduce<SumOp>(make_float2(s1, s2), g, scratch, 0, parity);
@@ -198,31 +209,41 @@ norm_bwd_kernel(const NormBwdParams p) {
     const float cc = LN ? -rstd * red.y * inv_n : 0.0f;
 
     // ---- pass 2: dx, dresidual, dw / db accumulation ----
+    auto pass2 = [&](auto full_tag) {
+      constexpr bool FULL = decltype(full_tag)::value;
 #pragma unroll
-    for (int k = 0; k < K; ++k) {
-      if (k < nkr) {
-        float x[VEC], dy[VEC], t[VEC], dx[VEC];
-        load_chunk_smem<DT, VEC>(x, sx + k * chunk_bytes, a.x_dtype);
-        load_chunk_smem<DT, VEC>(dy, sx + in_bytes + k * chunk_bytes, a.dout_dtype);
-        if constexpr (LN) vadd_s<VEC>(x, x, neg_mean);
-        vmul<VEC>(t, dy, w[k]);
-        vfma_ss<VEC>(dx, t, ca, cc);      // t * a + c
-        vfma_s<VEC>(dx, x, cb, dx);       // + xc * b
-        vmul<VEC>(t, dy, x);              // dout * xc
-        vfma_s<VEC>(dw[k], t, ca, dw[k]); // dw += (dout * xc) * rstd
-        if constexpr (DB) vadd<VEC>(db[k], db[k], dy);
-        if (has_dres_out) {
-          float dr[VEC];
-          load_chunk_smem<DT, VEC>(dr, sx + 2 * in_bytes + k * chunk_bytes, a.dresidual_out_dtype);
-          vadd<VEC>(dx, dx, dr);
+      for (int k = 0; k < K; ++k) {
+        if (FULL || k < nkr) {
+          float x[VEC], dy[VEC], t[VEC], dx[VEC];
+          load_chunk_smem<DT, VEC>(x, sx + k * chunk_bytes, a.x_dtype);
+          load_chunk_smem<DT, VEC>(dy, sx + in_bytes + k * chunk_bytes, a.dout_dtype);
+          if constexpr (LN) vadd_s<VEC>(x, x, neg_mean);
+          vmul<VEC>(t, dy, w[k]);
+          vfma_ss<VEC>(dx, t, ca, cc);       // t * a + c
+          vfma_s<VEC>(dx, x, cb, dx);        // + xc * b
+          vmul<VEC>(t, dy, x);               // dout * xc
+          vfma_s<VEC>(dw[k], t, ca, dw[k]);  // dw += (dout * xc) * rstd
+          if constexpr (DB) vadd<VEC>(db[k], db[k], dy);
+          if constexpr (!FULL) {
+            if (has_dres_out) {
+              float dr[VEC];
+              load_chunk_smem<DT, VEC>(dr, sx + 2 * in_bytes + k * chunk_bytes,
+                                       a.dresidual_out_dtype);
+              vadd<VEC>(dx, dx, dr);
+            }
+          }
+          store_chunk_p<DT, VEC>(dxp + k * step_dx, dx, a.dx_dtype);
+          if constexpr (!FULL) {
+            if (a.dresidual != nullptr)
+              store_chunk_p<DT, VEC>(reinterpret_cast<char*>(a.dresidual) +
+                                         (row * a.dresidual_row_stride + colbase) * esz_dr +
+                                         k * step_dr,
+                                     dx, a.dresidual_dtype);
+          }
         }
-        store_chunk_p<DT, VEC>(dxp + k * step_dx, dx, a.dx_dtype);
-        if (a.dresidual != nullptr)
-          store_chunk_p<DT, VEC>(reinterpret_cast<char*>(a.dresidual) +
-                                     (row * a.dresidual_row_stride + colbase) * esz_dr + k * step_dr,
-                                 dx, a.dresidual_dtype);
       }
-    }
+    };
+    if (full) pass2(std::true_type{}); else pass2(std::false_type{});
   }
   if (first && p.cluster_n > 1) cluster_wait();
   cp_async_wait<0>();
@@ -365,7 +386,7 @@ static int plan_norm_bwd(int64_t N, int vec, bool uniform, int x_dtype, bool has
   const ElemCaps caps = uniform ? ElemCaps{vec == 8 ? 64 : 32, 16, 8}
                                 : ElemCaps{dyn, dyn < 16 ? dyn : 16, dyn < 8 ? dyn : 8};
   const int64_t pref = uniform ? (vec == 8 ? 8192 : 4096) : 2048;
-  if (int rc = plan_rows("norm_bwd", N, vec, caps, pref, 2, 256, cfg, &out->rows)) return rc;
+  if (int rc = plan_rows("norm_bwd", N, vec, caps, pref, 4, 128, cfg, &out->rows)) return rc;
   out->uniform = uniform;
   out->n_in = has_dres_out ? 3 : 2;
   const int slot = uniform ? 16 : 4 * vec;
@@ -373,7 +394,7 @@ static int plan_norm_bwd(int64_t N, int vec, bool uniform, int x_dtype, bool has
   // Ring depth: as deep as shared memory allows (leaving room for a second CTA on the SM when
   // the stage is small), at most 4 by default.
   const size_t budget = (size_t)dev->max_smem_optin - 8192;  // static reduction scratch + margin
-  int stages = cfg.stages > 0 ? cfg.stages : 4;
+  int stages = cfg.stages > 0 ? cfg.stages : 2;  // two CTAs per SM beat a deeper ring
   if (stages > kMaxStages) stages = kMaxStages;
   while (stages > 1 && stage_bytes * stages > budget) --stages;
   if (stage_bytes * stages > budget)

@@ -32,7 +32,7 @@ struct NormFwdParams {
 template <int DT, int VEC, int K, bool LN, bool RAW, bool STAGED>
 __global__ void __launch_bounds__(RAW ? (K * VEC > 32 ? 256 : (K * VEC > 16 ? 512 : 1024))
                                       : (K * VEC > 32 ? 256 : (K * VEC > 16 ? 512 : 1024)),
-                                  (RAW && K * VEC > 32) ? 2 : 1)
+                                  (K * VEC > 32) ? 2 : 1)
 norm_fwd_kernel(const NormFwdParams p) {
   extern __shared__ __align__(16) unsigned char smem_params[];
   __shared__ ReduceScratch scratch;
@@ -62,8 +62,8 @@ norm_fwd_kernel(const NormFwdParams p) {
             step_ro = cstride * esz_ro;
 
   // Stage this CTA's column slice of (weight + weight_offset) and of the bias in shared memory as
-  // fp32 (ones / zeros when absent), chunk c at slot c, so that the per-row epilogue needs no
-  // dtype dispatch, no presence checks and no global loads.  Slices too large for a useful
+  // fp32 (ones when there is no weight), chunk c at slot c, so that the per-row epilogue needs no
+  // dtype dispatch and no global loads.  Slices too large for a useful
   // occupancy are read from global memory (L1/L2) instead.
   const bool has_w = a.weight != nullptr;
   const bool has_b = a.bias != nullptr;
@@ -99,9 +99,11 @@ norm_fwd_kernel(const NormFwdParams p) {
 #pragma unroll
       for (int i = 0; i < VEC; ++i)
         w_smem[param_index(c, i)] = has_w ? pv[i] + a.weight_offset : 1.0f;
-      if (has_b) load_chunk<kDynDT, VEC, false>(pv, a.bias, wrow + col0 + c * VEC, a.bias_dtype);
+      if (has_b) {  // the bias slice exists only when there is a bias
+        load_chunk<kDynDT, VEC, false>(pv, a.bias, wrow + col0 + c * VEC, a.bias_dtype);
 #pragma unroll
-      for (int i = 0; i < VEC; ++i) b_smem[param_index(c, i)] = has_b ? pv[i] : 0.0f;
+        for (int i = 0; i < VEC; ++i) b_smem[param_index(c, i)] = pv[i];
+      }
     }
     __syncthreads();
   }
@@ -233,7 +235,12 @@ norm_fwd_kernel(const NormFwdParams p) {
       for (int k = 0; k < K; ++k) {
         float w[VEC], b[VEC], y[VEC], xc[VEC];
         load_param(w, w_smem, chunk0 + k * p.tpr);
-        load_param(b, b_smem, chunk0 + k * p.tpr);
+        if (has_b) {
+          load_param(b, b_smem, chunk0 + k * p.tpr);
+        } else {
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) b[i] = 0.0f;
+        }
         if constexpr (RAW) {
           forget_values(rx[k]);
           unpack_chunk<DT, VEC>(xc, rx[k], a.x_dtype);
@@ -371,7 +378,11 @@ extern "C" int qb_norm_fwd(const qb_norm_fwd_args* args, qb_stream_t stream) {
   const ElemCaps caps = raw ? ElemCaps{128, 32, 16, 16}
                             : (uniform ? ElemCaps{64, 32, 16} : ElemCaps{32, 32, 16});
   const int64_t pref = raw ? 32768 : ((uniform && vec == 8) ? 16384 : 8192);
-  if (int rc = plan_rows("norm_fwd", a.N, vec, caps, pref, raw ? 16 : 8, 128, a.cfg, &plan))
+  // Packed rows: 16 chunks per thread (one warp per 4096-element row) for short rows, 8 from
+  // 8192 elements on; fp32-held rows 8.
+  const int k_target = (raw && a.N < 8192) ? 16 : 8;
+  if (int rc = plan_rows("norm_fwd", a.N, vec, caps, pref, k_target, raw && a.N >= 8192 ? 256 : 128,
+                         a.cfg, &plan))
     return rc;
   const int K = plan.K;
   const int threads = plan.threads;
@@ -385,7 +396,7 @@ extern "C" int qb_norm_fwd(const qb_norm_fwd_args* args, qb_stream_t stream) {
   p.num_tiles = ceil_div(a.M, p.rows_per_cta);
   // fp32 (weight + offset) and bias slices of this CTA's columns (ones / zeros when absent), if
   // small enough to leave room for several CTAs per SM.
-  size_t smem = static_cast<size_t>(plan.tpr) * plan.K * vec * 8;
+  size_t smem = static_cast<size_t>(plan.tpr) * plan.K * vec * 4 * (a.bias ? 2 : 1);
   p.stage_params = smem <= 64 * 1024;
   if (!p.stage_params) smem = 0;
   // Persistent grid: exactly the CTAs that are resident at once, each walking over row tiles (so

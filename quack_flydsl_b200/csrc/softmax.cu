@@ -248,9 +248,9 @@ static int softmax_dispatch(SoftmaxParams& p, bool uniform, int vec, const qb_la
   const bool packed = raw || (BWD && uniform);
   ElemCaps caps = packed ? ElemCaps{BWD ? 64 : 128, 64, BWD ? 16 : 32, BWD ? 8 : 16}
                          : (uniform ? ElemCaps{64, 64, 16} : ElemCaps{32, 32, 16});
-  const int64_t pref = packed ? 32768 : ((uniform && vec == 8) ? 16384 : 8192);
+  const int64_t pref = (packed && !BWD) ? 32768 : ((uniform && vec == 8) ? 16384 : 8192);
   if (int rc = plan_rows(BWD ? "softmax_bwd" : "softmax_fwd", p.N, vec, caps, pref,
-                         (packed && !BWD) ? 16 : 8, 128, cfg, &plan))
+                         BWD ? 4 : (packed ? 16 : 8), 128, cfg, &plan))
     return rc;
   p.tpr = plan.tpr;
   p.rows_per_cta = plan.rows_per_cta;

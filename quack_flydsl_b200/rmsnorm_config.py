@@ -31,7 +31,7 @@ class RmsNormFwdConfig:
         """The configuration the C launcher's heuristic picks for an aligned row of N elements."""
         vec = 128 // dtype_width
         threads, tpr, cluster_n = _plan(N, vec, pref_elems=16384 if vec == 8 else 8192,
-                                        k_target=4, caps=(64, 64, 16))
+                                        k_target=8, caps=(64, 32, 16), default_threads=128)
         return cls(num_threads=threads, threads_per_row=tpr, cluster_n=cluster_n)
 
 
@@ -51,7 +51,8 @@ class RmsNormBwdConfig:
                                   num_acc: int = 1) -> "RmsNormBwdConfig":
         vec = 128 // max(dtype_width, dout_width or dtype_width)
         threads, tpr, cluster_n = _plan(N, vec, pref_elems=8192 if vec == 8 else 4096,
-                                        k_target=2, caps=(64 if vec == 8 else 32, 16, 8))
+                                        k_target=4, caps=(64 if vec == 8 else 32, 16, 8),
+                                        default_threads=128)
         return cls(num_threads=threads, threads_per_row=tpr, cluster_n=cluster_n)
 
 
@@ -123,7 +124,7 @@ def get_sm_count(N: int, device, dtype: Optional[torch.dtype] = None) -> int:
     sms = props.multi_processor_count
     width = 32 if dtype == torch.float32 else 16
     cfg = RmsNormBwdConfig.from_analytical_heuristic(N, width)
-    per_sm = 2 if cfg.num_threads <= 512 and N * (width // 8) <= 8192 else 1
+    per_sm = 2 if cfg.num_threads <= 256 else 1
     return max(1, (sms * per_sm) // cfg.cluster_n)
 
 

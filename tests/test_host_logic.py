@@ -115,12 +115,15 @@ def test_config_dataclasses_and_search_spaces():
     assert all(c.threads_per_row <= c.num_threads for c in get_all_fwd_configs())
     assert len(get_all_bwd_configs()) > len(get_all_fwd_configs())
     h = RmsNormFwdConfig.from_analytical_heuristic(8192, 16)
-    assert (h.num_threads, h.threads_per_row, h.cluster_n) == (256, 256, 1)
+    assert (h.num_threads, h.threads_per_row, h.cluster_n) == (128, 128, 1)
     assert RmsNormFwdConfig.from_analytical_heuristic(65536, 16).cluster_n == 4
-    assert RmsNormFwdConfig.from_analytical_heuristic(262144, 16).cluster_n == 8
+    assert RmsNormFwdConfig.from_analytical_heuristic(262144, 16).cluster_n == 16
     hb = RmsNormBwdConfig.from_analytical_heuristic(8192, 16, 16)
-    assert (hb.num_threads, hb.threads_per_row, hb.cluster_n) == (512, 512, 1)
+    assert (hb.num_threads, hb.threads_per_row, hb.cluster_n) == (256, 256, 1)
     assert RmsNormBwdConfig.from_analytical_heuristic(262144, 16, 16).cluster_n == 16
+    # short rows: several rows per CTA
+    hs = RmsNormFwdConfig.from_analytical_heuristic(256, 16)
+    assert hs.threads_per_row < hs.num_threads
 
 
 def test_selection_cache_counts_specialisations():
