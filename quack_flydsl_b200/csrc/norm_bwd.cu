@@ -386,7 +386,7 @@ static int plan_norm_bwd(int64_t N, int vec, bool uniform, int x_dtype, bool has
   const ElemCaps caps = uniform ? ElemCaps{vec == 8 ? 64 : 32, 16, 8}
                                 : ElemCaps{dyn, dyn < 16 ? dyn : 16, dyn < 8 ? dyn : 8};
   const int64_t pref = uniform ? (vec == 8 ? 8192 : 4096) : 2048;
-  if (int rc = plan_rows("norm_bwd", N, vec, caps, pref, 4, 128, cfg, &out->rows)) return rc;
+  if (int rc = plan_rows("norm_bwd", N, vec, caps, pref, 8, 128, cfg, &out->rows)) return rc;
   out->uniform = uniform;
   out->n_in = has_dres_out ? 3 : 2;
   const int slot = uniform ? 16 : 4 * vec;

@@ -51,7 +51,7 @@ class RmsNormBwdConfig:
                                   num_acc: int = 1) -> "RmsNormBwdConfig":
         vec = 128 // max(dtype_width, dout_width or dtype_width)
         threads, tpr, cluster_n = _plan(N, vec, pref_elems=8192 if vec == 8 else 4096,
-                                        k_target=4, caps=(64 if vec == 8 else 32, 16, 8),
+                                        k_target=8, caps=(64 if vec == 8 else 32, 16, 8),
                                         default_threads=128)
         return cls(num_threads=threads, threads_per_row=tpr, cluster_n=cluster_n)
 

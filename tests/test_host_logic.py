@@ -119,7 +119,7 @@ def test_config_dataclasses_and_search_spaces():
     assert RmsNormFwdConfig.from_analytical_heuristic(65536, 16).cluster_n == 4
     assert RmsNormFwdConfig.from_analytical_heuristic(262144, 16).cluster_n == 16
     hb = RmsNormBwdConfig.from_analytical_heuristic(8192, 16, 16)
-    assert (hb.num_threads, hb.threads_per_row, hb.cluster_n) == (256, 256, 1)
+    assert (hb.num_threads, hb.threads_per_row, hb.cluster_n) == (128, 128, 1)
     assert RmsNormBwdConfig.from_analytical_heuristic(262144, 16, 16).cluster_n == 16
     # short rows: several rows per CTA
     hs = RmsNormFwdConfig.from_analytical_heuristic(256, 16)
