@@ -293,6 +293,86 @@ def suite(dev, peak) -> dict:
     return res
 
 
+def run_only(args) -> None:
+    """One kernel on a (small) case: ``--only NAME [--rows M] [--cols N] [--iters I]``.  Used for
+    Nsight Compute captures and quick checks; prints one JSON line with the mean device time."""
+    import importlib
+
+    rn = importlib.import_module("quack_flydsl_b200.rmsnorm")
+    sm = importlib.import_module("quack_flydsl_b200.softmax")
+    ce = importlib.import_module("quack_flydsl_b200.cross_entropy")
+    from quack_flydsl_b200.rmsnorm_config import get_sm_count
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    bf = torch.bfloat16
+    g = torch.Generator(device=dev).manual_seed(0)
+    name = args.only
+    defaults = {"rms_fwd": (12288, 8192), "rms_bwd": (12288, 8192), "ln_fwd": (24576, 4096),
+                "ln_bwd": (24576, 4096), "softmax_fwd": (24576, 4096), "softmax_bwd": (24576, 4096),
+                "ce_fwd": (2048, 128256), "ce_bwd": (1024, 128256)}
+    if name not in defaults:
+        raise SystemExit(f"--only must be one of {sorted(defaults)}")
+    M = args.rows or defaults[name][0]
+    N = args.cols or defaults[name][1]
+
+    def randn(*shape, scale=1.0, shift=0.0):
+        return (shift + scale * torch.randn(*shape, device=dev, generator=g)).to(bf)
+
+    if name in ("rms_fwd", "rms_bwd"):
+        x, res, w = randn(M, N), randn(M, N), randn(N, scale=0.1, shift=1.0)
+        out, ro = torch.empty_like(x), torch.empty_like(x)
+        rstd = torch.empty(M, device=dev)
+        fwd = lambda: rn._rmsnorm_fwd(x, w, out, None, rstd, None, res, ro, EPS)  # noqa: E731
+        fwd()
+        if name == "rms_fwd":
+            fn, nbytes = fwd, fwd_bytes(M, N)
+        else:
+            dout, dx = randn(M, N), torch.empty_like(x)
+            P = get_sm_count(N, dev, bf)
+            dwp = torch.empty(P, N, device=dev)
+            fn = lambda: rn._rmsnorm_bwd(ro, w, dout, rstd, dx, dwp, None, None, None, P)  # noqa: E731
+            nbytes = bwd_bytes(M, N)
+    elif name in ("ln_fwd", "ln_bwd"):
+        x, w, b = randn(M, N, shift=0.5), randn(N, scale=0.1, shift=1.0), randn(N, scale=0.1)
+        out = torch.empty_like(x)
+        rstd, mean = torch.empty(M, device=dev), torch.empty(M, device=dev)
+        fwd = lambda: rn._rmsnorm_fwd(x, w, out, b, rstd, mean, None, None, 1e-5, True)  # noqa: E731
+        fwd()
+        if name == "ln_fwd":
+            fn, nbytes = fwd, 2 * M * N * 2 + 2 * N * 2 + 2 * M * 4
+        else:
+            dout, dx = randn(M, N), torch.empty_like(x)
+            P = get_sm_count(N, dev, bf)
+            dwp, dbp = torch.empty(P, N, device=dev), torch.empty(P, N, device=dev)
+            fn = lambda: rn._rmsnorm_bwd(x, w, dout, rstd, dx, dwp, dbp, None, None, P, mean, True)  # noqa: E731
+            nbytes = 3 * M * N * 2 + 2 * M * 4 + N * 2 + 2 * N * 2
+    elif name in ("softmax_fwd", "softmax_bwd"):
+        x, y = randn(M, N, scale=3.0), torch.empty(M, N, device=dev, dtype=bf)
+        sm._softmax_fwd(x, y)
+        if name == "softmax_fwd":
+            fn, nbytes = (lambda: sm._softmax_fwd(x, y)), 2 * M * N * 2
+        else:
+            dy, dx = randn(M, N), torch.empty_like(x)
+            fn, nbytes = (lambda: sm._softmax_backward(dy, y, dx)), 3 * M * N * 2
+    else:
+        x = randn(M, N, scale=2.0)
+        t = torch.randint(0, N, (M,), device=dev, generator=g)
+        t[torch.rand(M, device=dev, generator=g) < 0.05] = -100
+        loss, lse = torch.empty(M, device=dev), torch.empty(M, device=dev)
+        ce.cross_entropy_fwd_out(x, t, None, loss, lse, None, None, -100)
+        if name == "ce_fwd":
+            fn = lambda: ce.cross_entropy_fwd_out(x, t, None, loss, lse, None, None, -100)  # noqa: E731
+            nbytes = M * N * 2 + 16 * M
+        else:
+            dx, dloss = torch.empty_like(x), torch.full((M,), 1.0 / M, device=dev)
+            fn = lambda: ce.cross_entropy_bwd_out(x, t, dloss, lse, dx, None, -100)  # noqa: E731
+            nbytes = 2 * M * N * 2 + 16 * M
+    ms = time_kernel(fn, iters=args.iters, warmup=1)
+    print(json.dumps({"only": name, "rows": M, "cols": N, "iters": args.iters, "ms": ms,
+                      "gbs": nbytes / ms / 1e6, "bytes": nbytes}), flush=True)
+
+
 def run_ours(args) -> None:
     import importlib
 
@@ -472,8 +552,14 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-suite", action="store_true", help="skip the per-kernel sweep of the other configurations")
+    ap.add_argument("--only", default=None, help="run one kernel on a small case (for ncu captures)")
+    ap.add_argument("--rows", type=int, default=0)
+    ap.add_argument("--cols", type=int, default=0)
+    ap.add_argument("--iters", type=int, default=3)
     args = ap.parse_args()
-    if args.impl == "reference":
+    if args.only:
+        run_only(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
