@@ -320,6 +320,38 @@ typedef struct qb_ce_combine_args {
 
 int qb_ce_combine(const qb_ce_combine_args* args, qb_stream_t stream);
 
+/*
+ * Norm backward without a caller-provided workspace.  No counterpart in the reference (there the
+ * caller always allocates dw_partial / db_partial with torch, quack/rmsnorm.py:1368-1379); added
+ * for hosts that may not allocate device memory: code running after an application's "memory is
+ * frozen" point, plugins that only receive input / output buffers, loops that cannot afford the
+ * device-wide synchronisation of cudaMalloc / cudaFree.
+ *
+ * Runs stage 1 (qb_norm_bwd) and stage 2 (qb_colsum) with the fp32 partial sums kept in a
+ * QB_STATIC_SCRATCH_BYTES array that is part of the library image on every GPU.  bwd.dw_partial,
+ * bwd.db_partial and bwd.num_partials are ignored.  dw / db receive the finished (H, N) parameter
+ * gradients in param_dtype; pass NULL for a gradient that is not wanted (db == NULL: no bias).
+ * Limit: H * N * (number of requested gradients) <= QB_STATIC_SCRATCH_BYTES / 4 /
+ * QB_STATIC_MIN_PARTIALS floats (65536 with the defaults, e.g. N = 32768 with dw and db);
+ * larger rows return QB_ERR_UNSUPPORTED.  The call allocates nothing.  Its first call on a device
+ * looks up the array's device address (cudaGetSymbolAddress) and should therefore be made once
+ * during start-up, before any stream capture.  All calls on a GPU share the array, which keeps
+ * the previous call's contents: calls that may overlap on the same GPU (other streams, other
+ * threads) race and must be ordered by the caller.
+ */
+#define QB_STATIC_SCRATCH_BYTES (16u << 20)
+#define QB_STATIC_MIN_PARTIALS 64
+
+typedef struct qb_norm_bwd_static_args {
+  qb_norm_bwd_args bwd;
+  void* dw;
+  void* db;
+  int32_t param_dtype;
+  int32_t pad0;
+} qb_norm_bwd_static_args;
+
+int qb_norm_bwd_static(const qb_norm_bwd_static_args* args, qb_stream_t stream);
+
 /* Fills *info for a CUDA device ordinal (-1 = current device). */
 int qb_query_device(int32_t device, qb_device_info* info);
 
@@ -332,7 +364,8 @@ int qb_abi_version(void);
 /*
  * sizeof() of an argument block as compiled into the library, so a foreign-language binding can
  * verify its struct layout before the first call.  which: 0 launch_cfg, 1 norm_fwd, 2 norm_bwd,
- * 3 colsum, 4 softmax_fwd, 5 softmax_bwd, 6 ce_fwd, 7 ce_bwd, 8 ce_combine, 9 device_info.
+ * 3 colsum, 4 softmax_fwd, 5 softmax_bwd, 6 ce_fwd, 7 ce_bwd, 8 ce_combine, 9 device_info,
+ * 10 norm_bwd_static.
  * Returns -1 for an unknown code.
  */
 int qb_sizeof_args(int32_t which);

@@ -79,6 +79,11 @@ class NormBwdArgs(Structure):
     ]
 
 
+class NormBwdStaticArgs(Structure):
+    _fields_ = [("bwd", NormBwdArgs), ("dw", c_void_p), ("db", c_void_p),
+                ("param_dtype", c_int32), ("pad0", c_int32)]
+
+
 class ColsumArgs(Structure):
     _fields_ = [
         ("partial", c_void_p), ("out", c_void_p), ("out_f32", c_void_p),
@@ -140,13 +145,14 @@ class CeCombineArgs(Structure):
 _SIZEOF_CODES = {
     0: LaunchCfg, 1: NormFwdArgs, 2: NormBwdArgs, 3: ColsumArgs, 4: SoftmaxFwdArgs,
     5: SoftmaxBwdArgs, 6: CeFwdArgs, 7: CeBwdArgs, 8: CeCombineArgs, 9: DeviceInfo,
+    10: NormBwdStaticArgs,
 }
 
 # every symbol include/quack_b200.h declares
 EXPORTED_SYMBOLS = (
     "qb_norm_fwd", "qb_norm_bwd", "qb_norm_bwd_num_partials", "qb_colsum", "qb_softmax_fwd",
     "qb_softmax_bwd", "qb_ce_fwd", "qb_ce_bwd", "qb_ce_combine", "qb_query_device",
-    "qb_last_error", "qb_abi_version", "qb_sizeof_args",
+    "qb_last_error", "qb_abi_version", "qb_sizeof_args", "qb_norm_bwd_static",
 )
 
 _LIB: Optional[ctypes.CDLL] = None
@@ -193,6 +199,7 @@ def lib() -> ctypes.CDLL:
         ("qb_norm_fwd", NormFwdArgs), ("qb_norm_bwd", NormBwdArgs), ("qb_colsum", ColsumArgs),
         ("qb_softmax_fwd", SoftmaxFwdArgs), ("qb_softmax_bwd", SoftmaxBwdArgs),
         ("qb_ce_fwd", CeFwdArgs), ("qb_ce_bwd", CeBwdArgs), ("qb_ce_combine", CeCombineArgs),
+        ("qb_norm_bwd_static", NormBwdStaticArgs),
     ):
         fn = getattr(cdll, name)
         fn.restype = ctypes.c_int

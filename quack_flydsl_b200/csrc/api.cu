@@ -133,6 +133,7 @@ extern "C" int qb_sizeof_args(int32_t which) {
     case 7: return (int)sizeof(qb_ce_bwd_args);
     case 8: return (int)sizeof(qb_ce_combine_args);
     case 9: return (int)sizeof(qb_device_info);
+    case 10: return (int)sizeof(qb_norm_bwd_static_args);
     default: return -1;
   }
 }
