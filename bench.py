@@ -35,6 +35,11 @@ EPS = 1e-6
 METRIC = "RMSNorm/LN/softmax/CE fwd+bwd HBM GB/s"
 WORKLOAD = "RMSNorm fwd+bwd bf16 [32768,8192] + residual (weight bf16, eps 1e-6), per GPU"
 NOMINAL_HBM_GBS = 8000.0
+# dram__bytes_read.sum + dram__bytes_write.sum of norm_fwd_kernel (RMSNorm forward with residual,
+# bf16, N = 8192) from one Nsight Compute capture at 12288 rows: 752,752,896 B per launch.  The
+# capture ran a smaller case than the 32768-row launch timed here; the kernel streams every row
+# once, so its traffic is proportional to the rows and the figure is kept per row.
+NCU_FWD_TRAFFIC_PER_ROW = 752752896 / 12288
 FALLBACK_PEAK_GBS = 6650.0
 
 
@@ -532,7 +537,10 @@ def run_ours(args) -> None:
             "roofline": {"bound": "hbm", "kernel": "norm_fwd_kernel (RMSNorm forward)",
                          "achieved": round(fwd_gbs, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(fwd_gbs / peak, 4), "peak_source": peak_src,
-                         "traffic": None},
+                         "traffic": round(NCU_FWD_TRAFFIC_PER_ROW * M),
+                         "traffic_note": "dram read+write of one ncu capture of this kernel at "
+                                         "12288 rows of the same N, scaled by rows (traffic is "
+                                         "proportional to rows; see profiles/)"},
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": launches,
