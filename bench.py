@@ -295,6 +295,9 @@ def suite(dev, peak) -> dict:
         M * N * 2 + 16 * M)
     rec("ce_bwd", time_kernel(lambda: ce.cross_entropy_bwd_out(x, t, dloss, lse, dxl, None, -100), iters=5, warmup=2),
         2 * M * N * 2 + 16 * M)
+    # loss + lse + dx in one call (the form chunked linear cross-entropy uses)
+    rec("ce_fwd_with_dx", time_kernel(lambda: ce.cross_entropy_fwd_out(x, t, None, loss, lse, dxl, None, -100), iters=5, warmup=2),
+        2 * M * N * 2 + 16 * M)
     return res
 
 
@@ -315,7 +318,8 @@ def run_only(args) -> None:
     name = args.only
     defaults = {"rms_fwd": (12288, 8192), "rms_bwd": (12288, 8192), "ln_fwd": (24576, 4096),
                 "ln_bwd": (24576, 4096), "softmax_fwd": (24576, 4096), "softmax_bwd": (24576, 4096),
-                "ce_fwd": (2048, 128256), "ce_bwd": (1024, 128256)}
+                "ce_fwd": (2048, 128256), "ce_bwd": (1024, 128256),
+                "ce_fwd_dx": (2048, 128256)}
     if name not in defaults:
         raise SystemExit(f"--only must be one of {sorted(defaults)}")
     M = args.rows or defaults[name][0]
@@ -365,10 +369,15 @@ def run_only(args) -> None:
         t = torch.randint(0, N, (M,), device=dev, generator=g)
         t[torch.rand(M, device=dev, generator=g) < 0.05] = -100
         loss, lse = torch.empty(M, device=dev), torch.empty(M, device=dev)
-        ce.cross_entropy_fwd_out(x, t, None, loss, lse, None, None, -100)
+        if name == "ce_bwd":
+            ce.cross_entropy_fwd_out(x, t, None, loss, lse, None, None, -100)
         if name == "ce_fwd":
             fn = lambda: ce.cross_entropy_fwd_out(x, t, None, loss, lse, None, None, -100)  # noqa: E731
             nbytes = M * N * 2 + 16 * M
+        elif name == "ce_fwd_dx":
+            dx = torch.empty_like(x)
+            fn = lambda: ce.cross_entropy_fwd_out(x, t, None, loss, lse, dx, None, -100)  # noqa: E731
+            nbytes = 2 * M * N * 2 + 16 * M
         else:
             dx, dloss = torch.empty_like(x), torch.full((M,), 1.0 / M, device=dev)
             fn = lambda: ce.cross_entropy_bwd_out(x, t, dloss, lse, dx, None, -100)  # noqa: E731

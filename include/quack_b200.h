@@ -49,8 +49,13 @@ typedef struct qb_launch_cfg {
   int32_t threads_per_row; /* threads cooperating on one row inside a CTA (power of two) */
   int32_t cluster_n;       /* CTAs of a thread-block cluster that share one row (1,2,4,8,16) */
   int32_t max_ctas;        /* cap on the grid (persistent kernels); 0 = heuristic */
-  int32_t stages;          /* shared-memory prefetch stages (norm backward); 0 = heuristic */
-  int32_t flags;           /* bit 0: keep rows as fp32 registers even where the packed 16-bit mode applies */
+  int32_t stages;          /* shared-memory prefetch stages (norm backward); chunks in flight per
+                              thread and input (streamed softmax: 4 / 8 forward, 2 / 4 backward);
+                              0 = heuristic */
+  int32_t flags;           /* measurement switches, 0 in production.
+                              bit 0: keep rows as fp32 registers even where the packed 16-bit mode applies
+                              bit 1: softmax: never use the streamed two-pass kernels for long rows
+                              bit 2 / bit 3: streamed softmax: plain L2 policy for pass 1 / pass 2 */
   int32_t reserved[2];
 } qb_launch_cfg;
 

@@ -108,6 +108,35 @@ __device__ __forceinline__ void ldg_stream(uint32_t* w, const void* p,
   }
 }
 
+// L2 cache policies for kernels that read a row twice (kind 0: evict last, 1: evict first,
+// 2: evict normal), and a 16-byte load that carries one.  PRED: predicated with zero fill, else
+// unconditional.
+__device__ __forceinline__ uint64_t l2_policy(int kind) {
+  uint64_t pol;
+  if (kind == 0) asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  else if (kind == 1) asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  else asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+template <bool PRED>
+__device__ __forceinline__ void ldg16_hint(uint32_t* w, const void* ptr, bool pred, uint64_t pol) {
+  if constexpr (PRED) {
+    const uint32_t pr = pred ? 1u : 0u;
+    asm volatile(
+        "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %5, 0;\n\t"
+        "mov.u32 %0, 0;\n\tmov.u32 %1, 0;\n\tmov.u32 %2, 0;\n\tmov.u32 %3, 0;\n\t"
+        "@q ld.global.L1::no_allocate.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %6;\n\t}"
+        : "=&r"(w[0]), "=&r"(w[1]), "=&r"(w[2]), "=&r"(w[3])
+        : "l"(ptr), "r"(pr), "l"(pol)
+        : "memory");
+  } else {
+    asm volatile("ld.global.L1::no_allocate.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
+                 : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3])
+                 : "l"(ptr), "l"(pol)
+                 : "memory");
+  }
+}
+
 // Predicated cached load (read-only path, default policy) for the small tensors that every CTA
 // re-reads: weight and bias.
 template <int BYTES>
@@ -288,6 +317,24 @@ __device__ __forceinline__ void unpack_chunk(float (&v)[VEC], const uint32_t* w,
     for (int i = 0; i < VEC; ++i) v[i] = __uint_as_float(w[i]);
   } else {
     unpack16<VEC>(v, w, d == QB_BF16);
+  }
+}
+
+// Maximum of the VEC packed 16-bit elements of a raw chunk (exact: the maximum of bf16 / fp16
+// values is one of them), without unpacking every element.
+template <int DT, int VEC>
+__device__ __forceinline__ float packed_max16(const uint32_t* w) {
+  static_assert(VEC >= 2 && (DT == QB_BF16 || DT == QB_F16), "packed 16-bit chunks only");
+  if constexpr (DT == QB_BF16) {
+    __nv_bfloat162 m = *reinterpret_cast<const __nv_bfloat162*>(&w[0]);
+#pragma unroll
+    for (int i = 1; i < VEC / 2; ++i) m = __hmax2(m, *reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+    return fmaxf(__low2float(m), __high2float(m));
+  } else {
+    __half2 m = *reinterpret_cast<const __half2*>(&w[0]);
+#pragma unroll
+    for (int i = 1; i < VEC / 2; ++i) m = __hmax2(m, *reinterpret_cast<const __half2*>(&w[i]));
+    return fmaxf(__low2float(m), __high2float(m));
   }
 }
 

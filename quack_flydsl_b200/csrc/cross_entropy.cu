@@ -6,6 +6,8 @@
 // it), so any row length runs in one CTA; a cluster splits long rows only when there are too few
 // rows to fill the GPU.  Backward follows quack/cross_entropy.py:463-546
 // (CrossEntropyBackward.kernel): a purely elementwise 2-D grid.
+#include <type_traits>
+
 #include "common.cuh"
 #include "host_common.h"
 
@@ -15,6 +17,7 @@ struct CeFwdParams {
   qb_ce_fwd_args a;
   int tpr, rows_per_cta, cluster_n, cols_per_cta;
   int64_t num_tiles;
+  int flags;  // qb_launch_cfg.flags
 };
 
 constexpr int kCeUnroll = 4;  // chunks in flight per thread and loop iteration
@@ -108,6 +111,150 @@ __global__ void __launch_bounds__(512) ce_fwd_kernel(const CeFwdParams p) {
     }
   }
   if (first && p.cluster_n > 1) cluster_wait();
+}
+
+// ---------------------------------------------------------------------------------------------
+// forward with dx in one launch: loss, lse and dx = w[t] * (softmax(x) - onehot)
+// ---------------------------------------------------------------------------------------------
+// The reference's forward kernel keeps the row in shared memory and writes dx from there
+// (quack/cross_entropy.py:240-265).  Vocabulary rows (64 ... 512 KB) do not fit, so here one CTA
+// streams its row twice: pass 1 (online log-sum-exp, as in ce_fwd_kernel) leaves the row in L2,
+// pass 2 re-reads it from L2 newest lines first and writes dx.  DRAM sees one read and one write
+// per logit, as in the reference.  dx may alias x: every chunk is read and written by the same
+// thread, and everything pass 1 needs from the row is read before pass 2 starts.
+// T threads share the row (T == blockDim.x), U chunks in flight per thread; blocks of T * U
+// chunks, all but possibly the last one full.
+template <int DT, int U, int T>
+__global__ void __launch_bounds__(T, (T >= 1024) ? 1 : (1024 / T)) ce_fwd_dx_kernel(const CeFwdParams p) {
+  static_assert(DT == QB_F32 || DT == QB_F16 || DT == QB_BF16, "concrete dtype required");
+  constexpr int VEC = DT == QB_F32 ? 4 : 8;
+  constexpr int kStep = T * 16;
+  constexpr int kBlockBytes = U * kStep;
+  __shared__ ReduceScratch scratch;
+  const qb_ce_fwd_args& a = p.a;
+  const RowGeom g = make_geom(T, 1);
+  const int N = static_cast<int>(a.N);
+  const int nchunks = N / VEC;
+  const int nfull = nchunks / (T * U);
+  const bool tail = nfull * (T * U) < nchunks;
+  const int tail_c0 = nfull * (T * U) + g.t;
+  const uint64_t keep = l2_policy((p.flags & 4) ? 2 : 0);
+  const uint64_t drop = l2_policy((p.flags & 8) ? 2 : 1);
+  int parity = 0;
+  for (int64_t row = blockIdx.x; row < a.M; row += gridDim.x) {
+    const char* xin = reinterpret_cast<const char*>(a.x) + (row * a.x_row_stride * (16 / VEC) + g.t * 16);
+    char* dxo = reinterpret_cast<char*>(a.dx) + (row * a.dx_row_stride * (16 / VEC) + g.t * 16);
+
+    // Row scalars (same address for all threads: broadcast loads), read before this row's dx
+    // is written because dx may alias x.
+    const int64_t tgt = load_index(a.target, row, a.target_dtype);
+    const bool ignored = tgt == a.ignore_index;
+    const int64_t local = tgt - a.col_offset;
+    const bool owned = !ignored && local >= 0 && local < a.N;
+    float gscale = 0.0f;  // w[target], 0 for ignored rows
+    if (!ignored) gscale = a.weight != nullptr ? load_scalar(a.weight, tgt, a.weight_dtype) : 1.0f;
+    const int tcol = owned ? static_cast<int>(local) : -1;
+    float tl = 0.0f;
+    if (g.t == 0 && !ignored) {
+      if (a.target_logit != nullptr) {
+        tl = a.target_logit_ndim == 2
+                 ? load_scalar(a.target_logit, row * a.target_logit_row_stride + tgt,
+                               a.target_logit_dtype)
+                 : load_scalar(a.target_logit, row, a.target_logit_dtype);
+      } else if (owned) {
+        tl = load_scalar(a.x, row * a.x_row_stride + local, a.x_dtype);
+      }
+    }
+
+    // ---- pass 1 ----
+    float m = neg_inf(), s = 0.0f;
+    ExpOffset off = exp_offset(m);
+    auto pass1 = [&](auto full_tag, const char* q, int c0) {
+      constexpr bool FULL = decltype(full_tag)::value;
+      uint32_t r[U][4];
+#pragma unroll
+      for (int u = 0; u < U; ++u) ldg16_hint<!FULL>(r[u], q + u * kStep, c0 + u * T < nchunks, keep);
+      float cm = neg_inf();
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (FULL || c0 + u * T < nchunks) {
+          if constexpr (DT == QB_F32) {
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) cm = fmaxf(cm, __uint_as_float(r[u][i]));
+          } else {
+            cm = fmaxf(cm, packed_max16<DT, VEC>(r[u]));
+          }
+        }
+      }
+      if (cm > m) {
+        const ExpOffset nw = exp_offset(cm);
+        s *= fast_exp2(nw.hi - off.hi);
+        m = cm;
+        off = nw;
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (FULL || c0 + u * T < nchunks) {
+          float v[VEC];
+          unpack_chunk<DT, VEC>(v, r[u], DT);
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) s += fast_exp2(fmaf(v[i], kLog2e, off.hi));
+        }
+      }
+    };
+    {
+      const char* q = xin;
+      for (int b = 0; b < nfull; ++b, q += kBlockBytes) pass1(std::true_type{}, q, 0);
+      if (tail) pass1(std::false_type{}, q, tail_c0);
+    }
+    s *= fast_exp2(off.lo);
+    const float2 ms = row_reduce<MaxSumExpOp>(make_float2(m, s), g, scratch, 0, parity);
+    parity ^= 1;
+    const float log_s = logf(ms.y);
+    const float lse = ms.x + log_s;
+    if (g.t == 0) {
+      if (a.lse != nullptr) a.lse[row] = lse;
+      if (a.loss != nullptr) a.loss[row] = ignored ? 0.0f : gscale * ((ms.x - tl) + log_s);
+      if (a.row_max != nullptr) a.row_max[row] = ms.x;
+      if (a.row_sumexp != nullptr) a.row_sumexp[row] = ms.y;
+      if (a.row_tgt != nullptr) a.row_tgt[row] = tl;
+    }
+
+    // ---- pass 2: dx, newest lines first ----
+    off = exp_offset(lse);
+    const float pscale = fast_exp2(off.lo) * gscale;
+    auto pass2 = [&](auto full_tag, const char* q, char* qo, int c0) {
+      constexpr bool FULL = decltype(full_tag)::value;
+      uint32_t r[U][4];
+#pragma unroll
+      for (int u = 0; u < U; ++u) ldg16_hint<!FULL>(r[u], q + u * kStep, c0 + u * T < nchunks, drop);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        float v[VEC], d[VEC];
+        unpack_chunk<DT, VEC>(v, r[u], DT);
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) d[i] = fast_exp2(fmaf(v[i], kLog2e, off.hi)) * pscale;
+        const unsigned rel = static_cast<unsigned>(tcol - (c0 + u * T) * VEC);
+        if (rel < static_cast<unsigned>(VEC)) {
+#pragma unroll
+          for (int i = 0; i < VEC; ++i)
+            if (rel == static_cast<unsigned>(i)) d[i] -= gscale;
+        }
+        if (FULL || c0 + u * T < nchunks) store_chunk_p<DT, VEC>(qo + u * kStep, d, DT);
+      }
+    };
+    {
+      const int64_t end = static_cast<int64_t>(nfull) * kBlockBytes;
+      if (tail) pass2(std::false_type{}, xin + end, dxo + end, tail_c0);
+      const char* q = xin + end;
+      char* qo = dxo + end;
+      for (int b = nfull - 1; b >= 0; --b) {
+        q -= kBlockBytes;
+        qo -= kBlockBytes;
+        pass2(std::true_type{}, q, qo, b * (T * U) + g.t);
+      }
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -281,6 +428,31 @@ static int run_ce_bwd(const qb_ce_bwd_args& a, cudaStream_t st) {
                                                      st);
 }
 
+template <int DT, int T>
+static int launch_ce_fwd_dx_t(const CeFwdParams& p, const DeviceFacts* dev, cudaStream_t st) {
+  auto kernel = ce_fwd_dx_kernel<DT, 8, T>;
+  const int occ = cached_occupancy(reinterpret_cast<const void*>(kernel), T, 0);
+  int64_t ctas = static_cast<int64_t>(dev->sm_count) * (occ > 0 ? occ : 1);
+  if (p.a.cfg.max_ctas > 0) ctas = p.a.cfg.max_ctas;
+  if (ctas > p.a.M) ctas = p.a.M;
+  // Evict-last marking in pass 1 only while the rows in flight fit comfortably in L2.
+  CeFwdParams q = p;
+  if (ctas * p.a.N * host_dtype_bytes(p.a.x_dtype) > (48LL << 20)) q.flags |= 4;
+  dim3 grid(static_cast<unsigned>(ctas), 1, 1);
+  return launch_kernel(kernel, grid, T, 0, 1, st, q, "ce_fwd (with dx)");
+}
+
+template <int DT>
+static int launch_ce_fwd_dx(const CeFwdParams& p, int threads, const DeviceFacts* dev,
+                            cudaStream_t st) {
+  switch (threads) {
+    case 256: return launch_ce_fwd_dx_t<DT, 256>(p, dev, st);
+    case 512: return launch_ce_fwd_dx_t<DT, 512>(p, dev, st);
+    case 1024: return launch_ce_fwd_dx_t<DT, 1024>(p, dev, st);
+    default: return set_error(QB_ERR_INVALID, "ce_fwd (with dx): num_threads must be 256, 512 or 1024");
+  }
+}
+
 }  // namespace qb
 
 using namespace qb;
@@ -331,6 +503,32 @@ extern "C" int qb_ce_fwd(const qb_ce_fwd_args* args, qb_stream_t stream) {
   vw.add_tensor(a.x, a.x_dtype, a.x_row_stride);
   const int vec = vw.vec;
   const bool uniform = vec == 16 / host_dtype_bytes(a.x_dtype);
+  if (a.dx != nullptr) {
+    // Vocabulary-sized rows with enough rows to give every SM one: loss, lse and dx in one
+    // launch that streams each row twice (the second time from L2).
+    VecWidth vd = vw;
+    vd.add_tensor(a.dx, a.x_dtype, a.dx_row_stride);
+    const int64_t row_bytes = a.N * host_dtype_bytes(a.x_dtype);
+    if (vd.vec == 16 / host_dtype_bytes(a.x_dtype) && a.cfg.cluster_n == 0 &&
+        !(a.cfg.flags & 2) && a.M >= dev->sm_count && row_bytes >= (64 << 10)) {
+      CeFwdParams p;
+      p.a = a;
+      p.tpr = 0;
+      p.rows_per_cta = 1;
+      p.cluster_n = 1;
+      p.cols_per_cta = static_cast<int>(a.N);
+      p.num_tiles = a.M;
+      p.flags = a.cfg.flags;
+      const int t = a.cfg.num_threads > 0
+                        ? a.cfg.num_threads
+                        : (row_bytes <= (96 << 10) ? 256 : (row_bytes <= (192 << 10) ? 512 : 1024));
+      switch (a.x_dtype) {
+        case QB_BF16: return launch_ce_fwd_dx<QB_BF16>(p, t, dev, st);
+        case QB_F16: return launch_ce_fwd_dx<QB_F16>(p, t, dev, st);
+        default: return launch_ce_fwd_dx<QB_F32>(p, t, dev, st);
+      }
+    }
+  }
   int threads = a.cfg.num_threads > 0 ? a.cfg.num_threads : 128;
   if (!is_pow2(threads) || threads < 32 || threads > 512)
     return set_error(QB_ERR_INVALID, "ce_fwd: bad num_threads %d", threads);
@@ -364,6 +562,7 @@ extern "C" int qb_ce_fwd(const qb_ce_fwd_args* args, qb_stream_t stream) {
   p.cluster_n = cluster_n;
   p.cols_per_cta = static_cast<int>(ceil_div(chunks, cluster_n) * vec);
   p.num_tiles = ceil_div(a.M, p.rows_per_cta);
+  p.flags = a.cfg.flags;
   const int64_t max_ctas =
       a.cfg.max_ctas > 0 ? a.cfg.max_ctas
                          : (cluster_n == 1 ? (int64_t)0x7fffffff

@@ -5,6 +5,8 @@
 // (SoftmaxBackward.kernel).  A row is read once, kept in registers, and written once; rows longer
 // than one CTA's register capacity are split over a thread-block cluster whose CTAs exchange
 // their partials through distributed shared memory.
+#include <type_traits>
+
 #include "common.cuh"
 #include "host_common.h"
 
@@ -20,25 +22,8 @@ struct SoftmaxParams {
   int dt0, dt1, dto;
   int tpr, rows_per_cta, cluster_n, cols_per_cta;
   int64_t num_tiles;
+  int flags;  // qb_launch_cfg.flags
 };
-
-// Maximum of the VEC packed 16-bit elements of a raw chunk (exact: the maximum of bf16 / fp16
-// values is one of them), without unpacking every element.
-template <int DT, int VEC>
-__device__ __forceinline__ float packed_max16(const uint32_t* w) {
-  static_assert(VEC >= 2 && (DT == QB_BF16 || DT == QB_F16), "packed 16-bit chunks only");
-  if constexpr (DT == QB_BF16) {
-    __nv_bfloat162 m = *reinterpret_cast<const __nv_bfloat162*>(&w[0]);
-#pragma unroll
-    for (int i = 1; i < VEC / 2; ++i) m = __hmax2(m, *reinterpret_cast<const __nv_bfloat162*>(&w[i]));
-    return fmaxf(__low2float(m), __high2float(m));
-  } else {
-    __half2 m = *reinterpret_cast<const __half2*>(&w[0]);
-#pragma unroll
-    for (int i = 1; i < VEC / 2; ++i) m = __hmax2(m, *reinterpret_cast<const __half2*>(&w[i]));
-    return fmaxf(__low2float(m), __high2float(m));
-  }
-}
 
 // RAW (16-bit inputs): the row stays packed in registers (twice the bytes in flight per register)
 // and is unpacked by each pass; the exponential is then evaluated twice per element (once for the
@@ -203,6 +188,156 @@ softmax_bwd_kernel(const SoftmaxParams p) {
 }
 
 // ---------------------------------------------------------------------------------------------
+// Long rows: two streamed passes per row with the row parked in L2 between them
+// ---------------------------------------------------------------------------------------------
+// A row that does not fit one CTA's registers is not split over a cluster here.  One CTA owns the
+// whole row and reads it twice: pass 1 streams it for the row statistic (online (max, sum-exp)
+// forward, sum(dy * y) backward) with an L2 evict-last policy, pass 2 streams it again -- in
+// reverse order, most recently touched lines first -- with an evict-first policy, computes the
+// result and writes it.  The grid is sized so that the rows in flight (resident CTAs x row bytes)
+// cover only a fraction of L2, which makes the second read an L2 hit: DRAM still sees one read
+// and one write per element, and no CTA ever waits on another one.
+// DT is one of the three concrete dtypes (all tensors share it, full 16-byte chunks); T threads
+// share one row (T == blockDim.x); U = chunks in flight per thread and input.  A row is walked in
+// blocks of T * U chunks; all blocks but possibly the last are full and take straight-line code
+// with compile-time address offsets.
+template <int DT, bool BWD, int U, int T>
+__global__ void __launch_bounds__(T, (T >= 1024) ? 1 : (1024 / T)) softmax_stream_kernel(const SoftmaxParams p) {
+  static_assert(DT == QB_F32 || DT == QB_F16 || DT == QB_BF16, "concrete dtype required");
+  constexpr int VEC = DT == QB_F32 ? 4 : 8;
+  constexpr int kStep = T * 16;           // bytes between a thread's chunks u and u + 1
+  constexpr int kBlockBytes = U * kStep;  // bytes of one block of the row
+  __shared__ ReduceScratch scratch;
+  const RowGeom g = make_geom(T, 1);
+  const int nchunks = p.N / VEC;
+  const int nfull = nchunks / (T * U);           // full blocks
+  const bool tail = nfull * (T * U) < nchunks;   // one more, partial, block
+  const int tail_c0 = nfull * (T * U) + g.t;     // this thread's first chunk of the partial block
+  const uint64_t keep = l2_policy((p.flags & 4) ? 2 : 0);
+  const uint64_t drop = l2_policy((p.flags & 8) ? 2 : 1);
+  int parity = 0;
+  for (int64_t row = blockIdx.x; row < p.M; row += gridDim.x) {
+    const char* in0 = reinterpret_cast<const char*>(p.in0) + (row * p.ld0 * (16 / VEC) + g.t * 16);
+    const char* in1 = BWD ? reinterpret_cast<const char*>(p.in1) + (row * p.ld1 * (16 / VEC) + g.t * 16)
+                          : nullptr;
+    char* out = reinterpret_cast<char*>(p.out) + (row * p.ldo * (16 / VEC) + g.t * 16);
+
+    float m = neg_inf(), s = 0.0f;  // forward: running max and sum 2^(x*log2e + off.hi)
+    ExpOffset off = exp_offset(m);
+    float dot = 0.0f;               // backward: sum(dy * y)
+
+    // ---- pass 1 ----
+    auto pass1 = [&](auto full_tag, const char* q0, const char* q1, int c0) {
+      constexpr bool FULL = decltype(full_tag)::value;
+      uint32_t r0[U][4];
+      uint32_t r1[BWD ? U : 1][4];
+#pragma unroll
+      for (int u = 0; u < U; ++u) ldg16_hint<!FULL>(r0[u], q0 + u * kStep, c0 + u * T < nchunks, keep);
+      if constexpr (BWD) {
+#pragma unroll
+        for (int u = 0; u < U; ++u) ldg16_hint<!FULL>(r1[u], q1 + u * kStep, c0 + u * T < nchunks, keep);
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          float v[VEC], y[VEC];
+          unpack_chunk<DT, VEC>(v, r0[u], DT);
+          unpack_chunk<DT, VEC>(y, r1[u], DT);  // padding chunks are zeros: they add nothing
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) dot = fmaf(v[i], y[i], dot);
+        }
+      } else {
+        // maximum of the whole block first, one re-basing of the partial sum per block
+        float cm = neg_inf();
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          if (FULL || c0 + u * T < nchunks) {
+            if constexpr (DT == QB_F32) {
+#pragma unroll
+              for (int i = 0; i < VEC; ++i) cm = fmaxf(cm, __uint_as_float(r0[u][i]));
+            } else {
+              cm = fmaxf(cm, packed_max16<DT, VEC>(r0[u]));
+            }
+          }
+        }
+        if (cm > m) {
+          const ExpOffset nw = exp_offset(cm);
+          s *= fast_exp2(nw.hi - off.hi);
+          m = cm;
+          off = nw;
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          if (FULL || c0 + u * T < nchunks) {
+            float v[VEC];
+            unpack_chunk<DT, VEC>(v, r0[u], DT);
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) s += fast_exp2(fmaf(v[i], kLog2e, off.hi));
+          }
+        }
+      }
+    };
+    {
+      const char* q0 = in0;
+      const char* q1 = in1;
+      for (int b = 0; b < nfull; ++b, q0 += kBlockBytes, q1 += kBlockBytes)
+        pass1(std::true_type{}, q0, q1, 0);
+      if (tail) pass1(std::false_type{}, q0, q1, tail_c0);
+    }
+
+    float scale = 0.0f;
+    if constexpr (BWD) {
+      dot = row_reduce<SumOp>(make_float2(dot, 0.f), g, scratch, 0, parity).x;
+    } else {
+      s *= fast_exp2(off.lo);
+      const float2 ms = row_reduce<MaxSumExpOp>(make_float2(m, s), g, scratch, 0, parity);
+      off = exp_offset(ms.x);
+      scale = ms.x == neg_inf() ? 0.0f : fast_exp2(off.lo) * (1.0f / ms.y);
+    }
+    parity ^= 1;
+
+    // ---- pass 2: newest lines first ----
+    auto pass2 = [&](auto full_tag, const char* q0, const char* q1, char* qo, int c0) {
+      constexpr bool FULL = decltype(full_tag)::value;
+      uint32_t r0[U][4];
+      uint32_t r1[BWD ? U : 1][4];
+#pragma unroll
+      for (int u = 0; u < U; ++u) ldg16_hint<!FULL>(r0[u], q0 + u * kStep, c0 + u * T < nchunks, drop);
+      if constexpr (BWD) {
+#pragma unroll
+        for (int u = 0; u < U; ++u) ldg16_hint<!FULL>(r1[u], q1 + u * kStep, c0 + u * T < nchunks, drop);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        float v[VEC], o[VEC];
+        unpack_chunk<DT, VEC>(v, r0[u], DT);
+        if constexpr (BWD) {
+          float y[VEC];
+          unpack_chunk<DT, VEC>(y, r1[u], DT);
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) o[i] = y[i] * (v[i] - dot);
+        } else {
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) o[i] = fast_exp2(fmaf(v[i], kLog2e, off.hi)) * scale;
+        }
+        if (FULL || c0 + u * T < nchunks) store_chunk_p<DT, VEC>(qo + u * kStep, o, DT);
+      }
+    };
+    {
+      const int64_t end = static_cast<int64_t>(nfull) * kBlockBytes;
+      if (tail) pass2(std::false_type{}, in0 + end, in1 + end, out + end, tail_c0);
+      const char* q0 = in0 + end;
+      const char* q1 = in1 + end;
+      char* qo = out + end;
+      for (int b = nfull - 1; b >= 0; --b) {
+        q0 -= kBlockBytes;
+        q1 -= kBlockBytes;
+        qo -= kBlockBytes;
+        pass2(std::true_type{}, q0, q1, qo, 0);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------------------------
 template <int DT, int VEC, bool BWD, bool RAW>
@@ -236,6 +371,70 @@ static int launch_softmax_v(const SoftmaxParams& p, int K, dim3 grid, int thread
   return set_error(QB_ERR_UNSUPPORTED, "%s: no kernel for %d chunks of %d per thread", name, K, VEC);
 }
 
+template <int DT, bool BWD, int U, int T>
+static int launch_softmax_stream_t(const SoftmaxParams& p, const qb_launch_cfg& cfg,
+                                   const DeviceFacts* dev, cudaStream_t st) {
+  auto kernel = softmax_stream_kernel<DT, BWD, U, T>;
+  const int occ = cached_occupancy(reinterpret_cast<const void*>(kernel), T, 0);
+  // Rows in flight (one per resident CTA) are what has to stay in L2 between the two passes.
+  int64_t ctas = static_cast<int64_t>(dev->sm_count) * (occ > 0 ? occ : 1);
+  if (cfg.max_ctas > 0) ctas = cfg.max_ctas;
+  if (ctas > p.M) ctas = p.M;
+  dim3 grid(static_cast<unsigned>(ctas), 1, 1);
+  // Pass 1 marks the row evict-last only while all rows in flight fit comfortably in L2; beyond
+  // that (measured: 76 MB in flight) the plain policy keeps more of the second pass in L2.
+  SoftmaxParams q = p;
+  const int64_t in_flight = ctas * static_cast<int64_t>(p.N) * host_dtype_bytes(p.dt0) * (BWD ? 2 : 1);
+  if (in_flight > (48LL << 20)) q.flags |= 4;
+  return launch_kernel(kernel, grid, T, 0, 1, st, q,
+                       BWD ? "softmax_bwd (streamed)" : "softmax_fwd (streamed)");
+}
+
+template <int DT, bool BWD, int U>
+static int launch_softmax_stream_u(const SoftmaxParams& p, const qb_launch_cfg& cfg,
+                                   const DeviceFacts* dev, int threads, cudaStream_t st) {
+  switch (threads) {
+    case 256: return launch_softmax_stream_t<DT, BWD, U, 256>(p, cfg, dev, st);
+    case 512: return launch_softmax_stream_t<DT, BWD, U, 512>(p, cfg, dev, st);
+    case 1024: return launch_softmax_stream_t<DT, BWD, U, 1024>(p, cfg, dev, st);
+    default:
+      return set_error(QB_ERR_INVALID, "softmax (streamed): num_threads must be 256, 512 or 1024");
+  }
+}
+
+template <bool BWD>
+static int launch_softmax_stream(SoftmaxParams& p, const qb_launch_cfg& cfg, const DeviceFacts* dev,
+                                 cudaStream_t st) {
+  // Measured on B200 (bf16, 1 GiB per tensor): the best CTA size walks a row in about two blocks
+  // of its chunks in flight -- forward 256 threads up to 48K elements, 512 up to 96K, else 1024
+  // (8 chunks in flight per thread); backward 512 threads up to 48K elements, else 1024 (2 chunks
+  // per thread and input).
+  const int64_t row_bytes = static_cast<int64_t>(p.N) * host_dtype_bytes(p.dt0);
+  int threads = cfg.num_threads;
+  if (threads <= 0) {
+    if (BWD) threads = row_bytes <= (96 << 10) ? 512 : 1024;
+    else threads = row_bytes <= (96 << 10) ? 256 : (row_bytes <= (192 << 10) ? 512 : 1024);
+  }
+  p.tpr = threads;
+  p.rows_per_cta = 1;
+  p.cluster_n = 1;
+  p.cols_per_cta = p.N;
+  p.num_tiles = p.M;
+  p.flags = cfg.flags;
+  // cfg.stages selects the chunks in flight per thread and input (default 8 forward, 2 backward).
+  const int u = cfg.stages > 0 ? cfg.stages : (BWD ? 2 : 8);
+#define QB_STREAM(DT)                                                                         \
+  if (u == (BWD ? 4 : 8)) return launch_softmax_stream_u<DT, BWD, (BWD ? 4 : 8)>(p, cfg, dev, threads, st); \
+  if (u == (BWD ? 2 : 4)) return launch_softmax_stream_u<DT, BWD, (BWD ? 2 : 4)>(p, cfg, dev, threads, st); \
+  return set_error(QB_ERR_INVALID, "softmax (streamed): unsupported chunks in flight %d", u);
+  switch (p.dt0) {
+    case QB_BF16: QB_STREAM(QB_BF16)
+    case QB_F16: QB_STREAM(QB_F16)
+    default: QB_STREAM(QB_F32)
+  }
+#undef QB_STREAM
+}
+
 template <bool BWD>
 static int softmax_dispatch(SoftmaxParams& p, bool uniform, int vec, const qb_launch_cfg& cfg,
                             cudaStream_t st) {
@@ -249,9 +448,21 @@ static int softmax_dispatch(SoftmaxParams& p, bool uniform, int vec, const qb_la
   ElemCaps caps = packed ? ElemCaps{BWD ? 64 : 128, 64, BWD ? 16 : 32, BWD ? 8 : 16}
                          : (uniform ? ElemCaps{64, 64, 16} : ElemCaps{32, 32, 16});
   const int64_t pref = (packed && !BWD) ? 32768 : ((uniform && vec == 8) ? 16384 : 8192);
-  if (int rc = plan_rows(BWD ? "softmax_bwd" : "softmax_fwd", p.N, vec, caps, pref,
-                         BWD ? 4 : (packed ? 16 : 8), 128, cfg, &plan))
-    return rc;
+  // Rows too long for one CTA's registers take the streamed two-pass kernel with the row parked
+  // in L2, unless the caller pinned a cluster size, set flag bit 1, or there are fewer rows than
+  // SMs (then splitting rows over clusters keeps more SMs busy).  The question "too long for one
+  // CTA" is put to the heuristic plan, whatever thread count the caller may have pinned.
+  const int k_target = BWD ? 4 : (packed ? 16 : 8);
+  const char* opname = BWD ? "softmax_bwd" : "softmax_fwd";
+  if (uniform && cfg.cluster_n == 0 && !(cfg.flags & 2) && p.M >= dev->sm_count) {
+    RowPlan probe;
+    const int rc = plan_rows(opname, p.N, vec, caps, pref, k_target, 128, qb_launch_cfg{}, &probe);
+    if (rc != QB_OK || probe.cluster_n > 1) {
+      clear_error();
+      return launch_softmax_stream<BWD>(p, cfg, dev, st);
+    }
+  }
+  if (int rc = plan_rows(opname, p.N, vec, caps, pref, k_target, 128, cfg, &plan)) return rc;
   p.tpr = plan.tpr;
   p.rows_per_cta = plan.rows_per_cta;
   p.cluster_n = plan.cluster_n;

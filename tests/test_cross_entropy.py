@@ -247,3 +247,42 @@ def test_cross_entropy_torch_compile_fullgraph():
     torch.testing.assert_close(loss.detach().cpu(), loss_ref, atol=ATOL, rtol=RTOL)
     dx_ref = oracle.cross_entropy_bwd_ref(x.detach().cpu().float(), target.cpu(), dloss.cpu(), lse_ref)
     assert_close_to_oracle(dx, dx_ref, torch.bfloat16, atol=1e-2, rtol=1.6e-2, max_ulp=None, what="dx")
+
+
+@pytest.mark.parametrize("inplace_backward", [False, True])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("N", [32768, 40008, 128256])
+def test_cross_entropy_fwd_with_grad_single_launch(N, dtype, inplace_backward, monkeypatch):
+    """With at least as many rows as SMs and vocabulary-sized rows, loss + lse + dx come from one
+    launch that streams every row twice.  It must agree with the oracle and with the two-kernel
+    path (flag bit 1), with class weights, ignored rows and the in-place gradient buffer."""
+    M = 300
+    x = (2.0 * torch.randn(M, N, device=DEV)).to(dtype)
+    target = torch.randint(0, N, (M,), device=DEV)
+    target[torch.rand(M, device=DEV) < 0.2] = -100
+    target[0], target[1] = 0, N - 1  # first and last column carry the one-hot term
+    weight = torch.rand(N, device=DEV) + 0.1
+    x_cpu = x.cpu()
+    x_work = x.clone()
+    loss, lse, dx = ce.cross_entropy_fwd(x_work, target, weight=weight, return_lse=True, return_dx=True,
+                                         inplace_backward=inplace_backward)
+    assert (dx is x_work) == inplace_backward
+    monkeypatch.setenv("QUACK_B200_CFG", "ce_fwd:0:0:0:0:0:2")
+    loss2, lse2, dx2 = ce.cross_entropy_fwd(x.clone(), target, weight=weight, return_lse=True, return_dx=True)
+    monkeypatch.delenv("QUACK_B200_CFG")
+    loss_ref, lse_ref = oracle.cross_entropy_ref(x_cpu, target.cpu(), weight=weight.cpu())
+    for l, s in ((loss, lse), (loss2, lse2)):
+        torch.testing.assert_close(l.cpu(), loss_ref, atol=ATOL, rtol=RTOL)
+        torch.testing.assert_close(s.cpu(), lse_ref, atol=ATOL, rtol=RTOL)
+    dx_ref = oracle.cross_entropy_bwd_ref(x_cpu.float(), target.cpu(), torch.ones(M), lse_ref, weight=weight.cpu())
+    at, rt = _dx_tol(dtype)
+    for d in (dx, dx2):
+        assert_close_to_oracle(d, dx_ref, dtype, atol=at, rtol=rt, max_ulp=None, what="dx")
+        assert (d[target == -100] == 0).all()
+    # explicit CTA sizes of the single-launch kernel
+    for threads in (256, 512, 1024):
+        monkeypatch.setenv("QUACK_B200_CFG", f"ce_fwd:{threads}")
+        l3, s3, d3 = ce.cross_entropy_fwd(x.clone(), target, weight=weight, return_lse=True, return_dx=True)
+        monkeypatch.delenv("QUACK_B200_CFG")
+        torch.testing.assert_close(s3.cpu(), lse_ref, atol=ATOL, rtol=RTOL)
+        assert_close_to_oracle(d3, dx_ref, dtype, atol=at, rtol=rt, max_ulp=None, what="dx")

@@ -107,3 +107,39 @@ def test_softmax_torch_compile_fullgraph():
     assert_close_to_oracle(out, oracle.softmax_ref(x.detach().cpu().float()), torch.bfloat16, what="y")
     dx_ref = oracle.softmax_bwd_ref(dy.cpu().float(), out.detach().cpu().float())
     assert_close_to_oracle(dx, dx_ref, torch.bfloat16, max_ulp=None, what="dx")
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_softmax_streamed_long_rows_match_cluster_path(dtype, monkeypatch):
+    """Rows longer than one CTA's registers take the streamed two-pass kernels when there are
+    at least as many rows as SMs; flag bit 1 forces the cluster kernels.  Both must agree with
+    the oracle and with each other, on strided rows with a ragged chunk count."""
+    M, N = 300, 65536 + 8 * 5
+    base = (2.0 * torch.randn(M, N + 64, device=DEV)).to(dtype)
+    x = base[:, :N]
+    x[3, 1000:] = float("-inf")  # masked tail
+    dy = torch.randn(M, N, device=DEV).to(dtype)
+    y_s = sm.softmax_fwd(x)
+    dx_s = sm.softmax_bwd(dy, y_s)
+    monkeypatch.setenv("QUACK_B200_CFG", "softmax_fwd:0:0:0:0:0:2;softmax_bwd:0:0:0:0:0:2")
+    y_c = sm.softmax_fwd(x)
+    dx_c = sm.softmax_bwd(dy, y_s)
+    assert not torch.equal(y_c, torch.zeros_like(y_c))
+    monkeypatch.delenv("QUACK_B200_CFG")
+    ref = oracle.softmax_ref(x.cpu().float())
+    for y in (y_s, y_c):
+        assert_close_to_oracle(y, ref, dtype, atol=TOL[dtype], rtol=TOL[dtype], what="y")
+    assert (y_s[3, 1000:] == 0).all()
+    dx_ref = oracle.softmax_bwd_ref(dy.cpu().float(), y_s.cpu().float())
+    for dx in (dx_s, dx_c):
+        assert_close_to_oracle(dx, dx_ref, dtype, atol=TOL[dtype], rtol=TOL[dtype], max_ulp=None, what="dx")
+    if dtype == torch.bfloat16:
+        assert oracle.bf16_ulp_diff(y_s.cpu(), y_c.cpu()).max() <= 1
+    # explicit thread counts / chunks in flight of the streamed kernels
+    for spec in ("softmax_fwd:512:0:0:0:4;softmax_bwd:512:0:0:0:2", "softmax_fwd:256:0:0:148:8;softmax_bwd:1024:0:0:0:4"):
+        monkeypatch.setenv("QUACK_B200_CFG", spec)
+        y = sm.softmax_fwd(x)
+        dx = sm.softmax_bwd(dy, y_s)
+        monkeypatch.delenv("QUACK_B200_CFG")
+        assert_close_to_oracle(y, ref, dtype, atol=TOL[dtype], rtol=TOL[dtype], what="y")
+        assert_close_to_oracle(dx, dx_ref, dtype, atol=TOL[dtype], rtol=TOL[dtype], max_ulp=None, what="dx")
