@@ -326,6 +326,26 @@ typedef struct qb_ce_combine_args {
 int qb_ce_combine(const qb_ce_combine_args* args, qb_stream_t stream);
 
 /*
+ * rstd[m] = rsqrt(sum_n x[m, n] * scale + eps) for an (M, N) matrix of partial sums of squares
+ * (fp32 / fp16 / bf16, unit column stride): the finalising step of a GEMM + RMSNorm pipeline.
+ * Replaces the compiled RmsFinalReduce kernel called by quack::rms_final_reduce_out
+ * (quack/rms_final_reduce.py:138-153, kernel :27-135).
+ */
+typedef struct qb_rms_final_reduce_args {
+  const void* x;
+  float* rstd; /* (M) fp32 */
+  int64_t M;
+  int64_t N;
+  int64_t x_row_stride;
+  float scale;
+  float eps;
+  int32_t x_dtype;
+  int32_t pad0;
+} qb_rms_final_reduce_args;
+
+int qb_rms_final_reduce(const qb_rms_final_reduce_args* args, qb_stream_t stream);
+
+/*
  * Norm backward without a caller-provided workspace.  No counterpart in the reference (there the
  * caller always allocates dw_partial / db_partial with torch, quack/rmsnorm.py:1368-1379); added
  * for hosts that may not allocate device memory: code running after an application's "memory is
@@ -370,7 +390,7 @@ int qb_abi_version(void);
  * sizeof() of an argument block as compiled into the library, so a foreign-language binding can
  * verify its struct layout before the first call.  which: 0 launch_cfg, 1 norm_fwd, 2 norm_bwd,
  * 3 colsum, 4 softmax_fwd, 5 softmax_bwd, 6 ce_fwd, 7 ce_bwd, 8 ce_combine, 9 device_info,
- * 10 norm_bwd_static.
+ * 10 norm_bwd_static, 11 rms_final_reduce.
  * Returns -1 for an unknown code.
  */
 int qb_sizeof_args(int32_t which);

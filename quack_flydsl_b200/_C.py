@@ -84,6 +84,12 @@ class NormBwdStaticArgs(Structure):
                 ("param_dtype", c_int32), ("pad0", c_int32)]
 
 
+class RmsFinalReduceArgs(Structure):
+    _fields_ = [("x", c_void_p), ("rstd", c_void_p), ("M", c_int64), ("N", c_int64),
+                ("x_row_stride", c_int64), ("scale", c_float), ("eps", c_float),
+                ("x_dtype", c_int32), ("pad0", c_int32)]
+
+
 class ColsumArgs(Structure):
     _fields_ = [
         ("partial", c_void_p), ("out", c_void_p), ("out_f32", c_void_p),
@@ -145,7 +151,7 @@ class CeCombineArgs(Structure):
 _SIZEOF_CODES = {
     0: LaunchCfg, 1: NormFwdArgs, 2: NormBwdArgs, 3: ColsumArgs, 4: SoftmaxFwdArgs,
     5: SoftmaxBwdArgs, 6: CeFwdArgs, 7: CeBwdArgs, 8: CeCombineArgs, 9: DeviceInfo,
-    10: NormBwdStaticArgs,
+    10: NormBwdStaticArgs, 11: RmsFinalReduceArgs,
 }
 
 # every symbol include/quack_b200.h declares
@@ -153,6 +159,7 @@ EXPORTED_SYMBOLS = (
     "qb_norm_fwd", "qb_norm_bwd", "qb_norm_bwd_num_partials", "qb_colsum", "qb_softmax_fwd",
     "qb_softmax_bwd", "qb_ce_fwd", "qb_ce_bwd", "qb_ce_combine", "qb_query_device",
     "qb_last_error", "qb_abi_version", "qb_sizeof_args", "qb_norm_bwd_static",
+    "qb_rms_final_reduce",
 )
 
 _LIB: Optional[ctypes.CDLL] = None
@@ -199,7 +206,7 @@ def lib() -> ctypes.CDLL:
         ("qb_norm_fwd", NormFwdArgs), ("qb_norm_bwd", NormBwdArgs), ("qb_colsum", ColsumArgs),
         ("qb_softmax_fwd", SoftmaxFwdArgs), ("qb_softmax_bwd", SoftmaxBwdArgs),
         ("qb_ce_fwd", CeFwdArgs), ("qb_ce_bwd", CeBwdArgs), ("qb_ce_combine", CeCombineArgs),
-        ("qb_norm_bwd_static", NormBwdStaticArgs),
+        ("qb_norm_bwd_static", NormBwdStaticArgs), ("qb_rms_final_reduce", RmsFinalReduceArgs),
     ):
         fn = getattr(cdll, name)
         fn.restype = ctypes.c_int

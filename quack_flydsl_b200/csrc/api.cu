@@ -134,6 +134,7 @@ extern "C" int qb_sizeof_args(int32_t which) {
     case 8: return (int)sizeof(qb_ce_combine_args);
     case 9: return (int)sizeof(qb_device_info);
     case 10: return (int)sizeof(qb_norm_bwd_static_args);
+    case 11: return (int)sizeof(qb_rms_final_reduce_args);
     default: return -1;
   }
 }

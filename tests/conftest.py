@@ -35,3 +35,8 @@ def softmax_ce_golden():
 def _seed():
     torch.manual_seed(0)
     yield
+
+
+@pytest.fixture(scope="session")
+def linear_ce_golden():
+    return torch.load(GOLDEN / "linear_ce_golden.pt", weights_only=True)

@@ -13,6 +13,10 @@ What is executed:
   reference function: ``F.layer_norm`` + autograd (tests/test_layernorm.py:64-74), ``F.softmax``
   + autograd (tests/test_softmax.py:53-57), ``F.cross_entropy`` / ``torch.logsumexp`` + autograd
   (tests/test_cross_entropy.py:51,64-66,288).
+* ``linear_cross_entropy_func_ref`` cut out of ``quack/linear_cross_entropy.py`` the same way and
+  run with autograd on CPU (fp32 upcast, as tests/test_linear_cross_entropy.py:33-35 does), and
+  the closed form the reference's ``rms_final_reduce`` test compares with
+  (tests/test_linear.py:793-803).
 Inputs are stored next to the outputs, so the fixtures do not depend on RNG reproducibility.
 """
 
@@ -138,6 +142,45 @@ def gen_cross_entropy() -> dict:
     return {"cross_entropy": cases}
 
 
+def load_linear_ce_ref(ref_root: Path):
+    from typing import Literal, Optional
+
+    src = (ref_root / "quack" / "linear_cross_entropy.py").read_text()
+    ns = {"torch": torch, "Tensor": torch.Tensor, "F": F, "Optional": Optional, "Literal": Literal}
+    for node in ast.parse(src).body:
+        if isinstance(node, ast.FunctionDef) and node.name == "linear_cross_entropy_func_ref":
+            exec(compile(ast.Module(body=[node], type_ignores=[]), "reference:linear_ce", "exec"), ns)
+    return ns["linear_cross_entropy_func_ref"]
+
+
+def gen_linear_ce(ref_root: Path) -> dict:
+    fn = load_linear_ce_ref(ref_root)
+    g = torch.Generator().manual_seed(4)
+    cases = []
+    for M, d, V, dt, red, ign in [(16, 64, 512, torch.bfloat16, "mean", False),
+                                  (24, 32, 1000, torch.bfloat16, "sum", True),
+                                  (8, 64, 640, torch.float32, "mean", True)]:
+        x = (0.1 * torch.randn(M, d, generator=g)).to(dt)
+        w = (torch.randn(V, d, generator=g) / d ** 0.5).to(dt)
+        target = torch.randint(0, V, (M,), generator=g)
+        ignore_index = V - 1 if ign else -100
+        if ign:
+            target[torch.rand(M, generator=g) < 0.3] = ignore_index
+            target[1] = ignore_index
+        xr, wr = x.float().clone().requires_grad_(), w.float().clone().requires_grad_()
+        loss = fn(xr, wr, None, target, ignore_index=ignore_index, reduction=red)
+        loss.backward()
+        cases.append(dict(x=x, weight=w, target=target, ignore_index=ignore_index, reduction=red,
+                          loss=loss.detach(), dx=xr.grad, dw=wr.grad))
+    rms = []
+    for M, N, dt in [(37, 1, torch.float32), (37, 16, torch.bfloat16), (5, 100, torch.float32)]:
+        x = torch.randn(M, N, generator=g).abs().to(dt)
+        scale, eps = 1.0 / 4096, 1e-6
+        rms.append(dict(x=x, scale=scale, eps=eps,
+                        rstd=torch.rsqrt(x.float().sum(dim=-1) * scale + eps)))
+    return {"linear_cross_entropy": cases, "rms_final_reduce": rms}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -147,7 +190,8 @@ def main() -> None:
     ref = load_reference_functions(Path(args.reference))
     torch.save({**gen_norm(ref), **gen_layernorm(ref)}, HERE / "norm_golden.pt")
     torch.save({**gen_softmax(), **gen_cross_entropy()}, HERE / "softmax_ce_golden.pt")
-    for f in ("norm_golden.pt", "softmax_ce_golden.pt"):
+    torch.save(gen_linear_ce(Path(args.reference)), HERE / "linear_ce_golden.pt")
+    for f in ("norm_golden.pt", "softmax_ce_golden.pt", "linear_ce_golden.pt"):
         print(f, (HERE / f).stat().st_size, "bytes")
 
 

@@ -134,3 +134,24 @@ def test_bf16_ulp_distance():
     a = torch.tensor([1.0, -1.0, 0.0, 3.0], dtype=torch.bfloat16)
     b = torch.tensor([1.0078125, -1.0078125, 0.0, 3.0], dtype=torch.bfloat16)
     assert oracle.bf16_ulp_diff(a, b).tolist() == [1, 1, 0, 0]
+
+
+def test_linear_cross_entropy_oracle_matches_reference_function(linear_ce_golden):
+    # fixtures: the reference's linear_cross_entropy_func_ref + autograd on fp32-upcast inputs
+    for c in linear_ce_golden["linear_cross_entropy"]:
+        loss, dx, dw = oracle.linear_cross_entropy_ref(
+            c["x"].float(), c["weight"].float(), c["target"], ignore_index=c["ignore_index"],
+            reduction=c["reduction"])
+        torch.testing.assert_close(loss.float(), c["loss"], atol=1e-5, rtol=1e-5)
+        torch.testing.assert_close(dx.float(), c["dx"], atol=1e-6, rtol=1e-4)
+        torch.testing.assert_close(dw.float(), c["dw"], atol=1e-6, rtol=1e-4)
+
+
+def test_rms_final_reduce_oracle_matches_closed_form(linear_ce_golden):
+    for c in linear_ce_golden["rms_final_reduce"]:
+        got = oracle.rms_final_reduce_ref(c["x"], c["scale"], c["eps"])
+        torch.testing.assert_close(got, c["rstd"], atol=0, rtol=1e-6)
+    # a single partial sum per row: rstd = rsqrt(x * scale + eps)
+    x = torch.tensor([[4.0], [0.0]])
+    torch.testing.assert_close(oracle.rms_final_reduce_ref(x, 0.25, 0.0)[0], torch.tensor(1.0))
+    torch.testing.assert_close(oracle.rms_final_reduce_ref(x, 0.25, 1e-6)[1], torch.tensor(1000.0), rtol=1e-5, atol=0)
