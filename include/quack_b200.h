@@ -54,8 +54,9 @@ typedef struct qb_launch_cfg {
                               0 = heuristic */
   int32_t flags;           /* measurement switches, 0 in production.
                               bit 0: keep rows as fp32 registers even where the packed 16-bit mode applies
-                              bit 1: softmax: never use the streamed two-pass kernels for long rows
-                              bit 2 / bit 3: streamed softmax: plain L2 policy for pass 1 / pass 2 */
+                              bit 1: never use the streamed two-pass kernels for long rows
+                              bit 2 / bit 3: streamed kernels: plain L2 policy for pass 1 / pass 2
+                              bit 4: norm forward: streamed two-pass kernel for any row length */
   int32_t reserved[2];
 } qb_launch_cfg;
 

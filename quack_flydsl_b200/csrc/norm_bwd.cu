@@ -144,6 +144,19 @@ norm_bwd_kernel(const NormBwdParams p) {
   };
 
   const int S = p.stages;
+  // Chunk slots beyond this thread's last chunk (rows whose length is not K full rounds of the
+  // row's threads, e.g. N = 6144 with 8 slots of 128 threads) are never copied into.  They are
+  // zeroed once, so that the straight-line passes can run over all K slots: a zero dout chunk
+  // adds nothing to any sum or accumulator, and only the dx store is predicated.
+  if constexpr (DT != kDynDT) {
+    for (int s = 0; s < S; ++s)
+      for (int j = 0; j < p.n_in; ++j)
+#pragma unroll
+        for (int k = 0; k < K; ++k)
+          if (k >= nk)
+            *reinterpret_cast<uint4*>(my_slot0 + s * stage_bytes + j * in_bytes + k * chunk_bytes) =
+                make_uint4(0u, 0u, 0u, 0u);
+  }
   for (int s = 0; s < S - 1; ++s) issue_tile(pidx + s * P, s);
 
   // Row statistics of the first tile; the next tile's are fetched one iteration ahead.
@@ -178,18 +191,20 @@ norm_bwd_kernel(const NormBwdParams p) {
     }
     cp_async_wait_dyn(S - 1);  // this tile's group has landed; S-1 younger groups may be in flight
 
-    // Both passes exist in two forms: FULL (every chunk of this thread exists and there is no
-    // residual-gradient stream: straight-line code, no per-chunk branches) and the general form.
-    // The row reduction between the passes stays outside of the per-thread choice, because it
-    // contains a barrier.
-    const bool full = (nkr == K) && !has_dres_out && a.dresidual == nullptr;
+    // Both passes exist in a general form and in a straight-line form without per-chunk branches
+    // for rows without a residual-gradient stream: mode 2 when all K chunks of this thread exist,
+    // mode 1 when some are padding (zeroed slots, only the dx store is predicated).  The row
+    // reduction between the passes stays outside of the per-thread choice: it contains a barrier.
+    const bool plain = !has_dres_out && a.dresidual == nullptr;
+    const int mode = !plain ? 0 : (nkr == K ? 2 : ((DT != kDynDT && m < a.M) ? 1 : 0));
 
     // ---- pass 1: S1 = sum(xc * t), S2 = sum(t) ----
     float s1v[VEC], s2v[VEC];
 #pragma unroll
     for (int i = 0; i < VEC; ++i) { s1v[i] = 0.0f; s2v[i] = 0.0f; }
     auto pass1 = [&](auto full_tag) {
-      constexpr bool FULL = decltype(full_tag)::value;
+      constexpr int MODE = decltype(full_tag)::value;
+      constexpr bool FULL = MODE != 0;
 #pragma unroll
       for (int k = 0; k < K; ++k) {
         if (FULL || k < nkr) {
@@ -203,7 +218,7 @@ norm_bwd_kernel(const NormBwdParams p) {
         }
       }
     };
-    if (full) pass1(std::true_type{}); else pass1(std::false_type{});
+    if (mode != 0) pass1(std::integral_constant<int, 2>{}); else pass1(std::integral_constant<int, 0>{});
     const float s1 = hsum<VEC>(s1v);
     const float s2 = LN ? hsum<VEC>(s2v) : 0.0f;
     if (first && p.cluster_n > 1) cluster_wait();
@@ -216,7 +231,8 @@ norm_bwd_kernel(const NormBwdParams p) {
 
     // ---- pass 2: dx, dresidual, dw / db accumulation ----
     auto pass2 = [&](auto full_tag) {
-      constexpr bool FULL = decltype(full_tag)::value;
+      constexpr int MODE = decltype(full_tag)::value;
+      constexpr bool FULL = MODE != 0;
 #pragma unroll
       for (int k = 0; k < K; ++k) {
         if (FULL || k < nkr) {
@@ -238,7 +254,7 @@ norm_bwd_kernel(const NormBwdParams p) {
               vadd<VEC>(dx, dx, dr);
             }
           }
-          store_chunk_p<DT, VEC>(dxp + k * step_dx, dx, a.dx_dtype);
+          if (MODE != 1 || k < nk) store_chunk_p<DT, VEC>(dxp + k * step_dx, dx, a.dx_dtype);
           if constexpr (!FULL) {
             if (a.dresidual != nullptr)
               store_chunk_p<DT, VEC>(reinterpret_cast<char*>(a.dresidual) +
@@ -249,7 +265,9 @@ norm_bwd_kernel(const NormBwdParams p) {
         }
       }
     };
-    if (full) pass2(std::true_type{}); else pass2(std::false_type{});
+    if (mode == 2) pass2(std::integral_constant<int, 2>{});
+    else if (mode == 1) pass2(std::integral_constant<int, 1>{});
+    else pass2(std::integral_constant<int, 0>{});
   }
   if (first && p.cluster_n > 1) cluster_wait();
   cp_async_wait<0>();

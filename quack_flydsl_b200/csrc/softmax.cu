@@ -28,19 +28,22 @@ struct SoftmaxParams {
 // RAW (16-bit inputs): the row stays packed in registers (twice the bytes in flight per register)
 // and is unpacked by each pass; the exponential is then evaluated twice per element (once for the
 // sum, once for the output).  Otherwise the exponentials are kept as fp32 registers.
-template <int DT, int VEC, int K, bool RAW>
+// TPR != 0 fixes the threads per row at compile time, which turns the chunk strides into
+// immediate offsets (the kernel is close to instruction-issue-bound: +4.6 % at N = 4096, bf16).
+template <int DT, int VEC, int K, bool RAW, int TPR = 0>
 __global__ void __launch_bounds__(RAW ? (K * VEC > 64 ? 256 : (K * VEC > 32 ? 512 : 1024))
                                       : (K * VEC > 16 ? 512 : 1024))
 softmax_fwd_kernel(const SoftmaxParams p) {
   __shared__ ReduceScratch scratch;
-  const RowGeom g = make_geom(p.tpr, p.cluster_n);
+  const int ptpr = TPR ? TPR : p.tpr;
+  const RowGeom g = make_geom(ptpr, p.cluster_n);
   if (p.cluster_n > 1) cluster_arrive();
   const int col0 = static_cast<int>(g.crank) * p.cols_per_cta;
   const int ncols = min(p.cols_per_cta, p.N - col0);
   const int colbase = col0 + g.t * VEC;
-  const int cstride = p.tpr * VEC;
+  const int cstride = ptpr * VEC;
   const int nchunks = ncols > 0 ? ncols / VEC : 0;
-  const int nk = nchunks > g.t ? min(K, (nchunks - g.t + p.tpr - 1) / p.tpr) : 0;
+  const int nk = nchunks > g.t ? min(K, (nchunks - g.t + ptpr - 1) / ptpr) : 0;
   const int64_t tile_stride = gridDim.x / p.cluster_n;
   int parity = 0;
   bool first = true;
@@ -362,9 +365,19 @@ static int launch_softmax_v(const SoftmaxParams& p, int K, dim3 grid, int thread
         if constexpr (BWD)
           return launch_kernel(softmax_bwd_kernel<DT, VEC, 16>, grid, threads, 0, p.cluster_n, st,
                                p, name);
-        else
+        else {
+          // compile-time geometry for the shapes the heuristics pick at N = 4096, 8192 and 16384
+          if constexpr (RAW) {
+            if (p.tpr == 32) return launch_kernel(softmax_fwd_kernel<DT, VEC, 16, RAW, 32>, grid, threads,
+                                                  0, p.cluster_n, st, p, name);
+            if (p.tpr == 64) return launch_kernel(softmax_fwd_kernel<DT, VEC, 16, RAW, 64>, grid, threads,
+                                                  0, p.cluster_n, st, p, name);
+            if (p.tpr == 128) return launch_kernel(softmax_fwd_kernel<DT, VEC, 16, RAW, 128>, grid,
+                                                   threads, 0, p.cluster_n, st, p, name);
+          }
           return launch_kernel(softmax_fwd_kernel<DT, VEC, 16, RAW>, grid, threads, 0,
                                p.cluster_n, st, p, name);
+        }
       }
   }
 #undef QB_CASE

@@ -149,3 +149,57 @@ def test_layernorm_empty():
     assert out.shape == (0, 1024)
     dx, dw, db = ln.layernorm_bwd(x, w, torch.empty_like(x), rstd, mean)
     assert (dw == 0).all() and (db == 0).all()
+
+
+rnm = importlib.import_module("quack_flydsl_b200.rmsnorm")
+
+
+@pytest.mark.parametrize("force", [False, True])
+def test_norm_forward_streamed_long_rows(force, monkeypatch):
+    """Long rows with at least one row per SM take the streamed two-pass forward kernels (flag
+    bit 4 forces them for shorter rows too).  RMSNorm with and without a residual, LayerNorm with
+    bias, parameters in the input dtype and in fp32, a ragged chunk count, and a large common
+    offset for the one-pass LayerNorm statistics."""
+    M = 160
+    N = 4104 if force else 65536 + 8 * 3
+    if force:
+        monkeypatch.setenv("QUACK_B200_CFG", "norm_fwd:0:0:0:0:0:16")
+    g = torch.Generator(device=DEV).manual_seed(3)
+    for dtype, wdtype in ((torch.bfloat16, torch.bfloat16), (torch.bfloat16, torch.float32),
+                          (torch.float32, torch.float32)):
+        x = torch.randn(M, N, device=DEV, generator=g).to(dtype)
+        res = torch.randn(M, N, device=DEV, generator=g).to(dtype)
+        w = (1 + 0.1 * torch.randn(N, device=DEV, generator=g)).to(wdtype)
+        b = (0.1 * torch.randn(N, device=DEV, generator=g)).to(wdtype)
+        xc, rc, wc, bc = x.cpu(), res.cpu(), w.cpu(), b.cpu()
+        # RMSNorm, no residual
+        out, _, rstd = rnm.rmsnorm_fwd(x, w, store_rstd=True)
+        assert_close_to_oracle(out, oracle.rmsnorm_ref(xc, wc, out_dtype=torch.float32), dtype,
+                               atol={torch.float32: 2e-5}.get(dtype), what="rms out")
+        torch.testing.assert_close(rstd.cpu(), oracle.rmsnorm_rstd_ref(xc), atol=0, rtol=1e-5)
+        # RMSNorm + residual (+ bias)
+        out, res_out, rstd = rnm.rmsnorm_fwd(x, w, bias=b, residual=res, store_rstd=True)
+        ref_out, ref_h = oracle.rmsnorm_ref(xc, wc, bias=bc, residual=rc, out_dtype=torch.float32,
+                                            residual_dtype=torch.float32)
+        assert torch.equal(res_out.cpu(), ref_h.to(dtype))
+        assert_close_to_oracle(out, ref_out, dtype, atol={torch.float32: 2e-5}.get(dtype), what="rms+res out")
+        torch.testing.assert_close(rstd.cpu(), oracle.rmsnorm_rstd_ref(xc, residual=rc), atol=0, rtol=1e-5)
+        # LayerNorm with bias through the op (any parameter dtype)
+        o = torch.empty_like(x)
+        rs, mn = torch.empty(M, device=DEV), torch.empty(M, device=DEV)
+        rnm._rmsnorm_fwd(x, w, o, b, rs, mn, None, None, 1e-5, True)
+        assert_close_to_oracle(o, oracle.layernorm_ref(xc, wc, bc, eps=1e-5), dtype,
+                               atol={torch.float32: 2e-5}.get(dtype), what="ln out")
+        torch.testing.assert_close(rs.cpu(), oracle.layernorm_rstd_ref(xc, eps=1e-5), atol=0, rtol=1e-5)
+        torch.testing.assert_close(mn.cpu(), oracle.layernorm_mean_ref(xc), atol=1e-6, rtol=1e-5)
+    # large common offset: x = 1000 + row * 100 + small pattern (fp32)
+    cols = torch.arange(N, device=DEV, dtype=torch.float32)
+    rows = torch.arange(M, device=DEV, dtype=torch.float32).unsqueeze(1)
+    x = 1000.0 + rows * 100.0 + ((cols % 17) - 8.0) / 8.0
+    w = torch.ones(N, device=DEV)
+    o = torch.empty_like(x)
+    rs, mn = torch.empty(M, device=DEV), torch.empty(M, device=DEV)
+    rnm._rmsnorm_fwd(x, w, o, None, rs, mn, None, None, 1e-5, True)
+    torch.testing.assert_close(mn.cpu(), oracle.layernorm_mean_ref(x.cpu()), atol=0, rtol=1e-6)
+    torch.testing.assert_close(rs.cpu(), oracle.layernorm_rstd_ref(x.cpu(), eps=1e-5), atol=0, rtol=2e-4)
+    torch.testing.assert_close(o.cpu(), oracle.layernorm_ref(x.cpu(), w.cpu(), eps=1e-5), atol=5e-3, rtol=1e-3)

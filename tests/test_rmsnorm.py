@@ -369,3 +369,60 @@ def test_rmsnorm_torch_compile_fullgraph():
     dx_ref, dw_ref, _ = oracle.rmsnorm_bwd_ref(x.detach().cpu(), w.detach().cpu(), dout.cpu(), rstd)
     assert_close_to_oracle(x.grad, dx_ref, torch.bfloat16, max_ulp=None, what="dx")
     torch.testing.assert_close(w.grad.cpu(), dw_ref, atol=2e-3 * M ** 0.5, rtol=1e-3)
+
+
+@pytest.mark.parametrize("N", [131072, 262144])
+def test_rmsnorm_large_tensor(N):
+    """More than 2**32 elements per tensor (reference: tests/test_rmsnorm.py:294-335): 64-bit row
+    offsets in the kernels.  Checked in row blocks against the fp32 formulas on the GPU."""
+    M = 32 * 1024
+    need = 2 * M * N * 2 + (2 << 30)
+    torch.cuda.empty_cache()
+    if need > torch.cuda.mem_get_info()[0] * 0.9:
+        pytest.skip("not enough free device memory")
+    g = torch.Generator(device=DEV).manual_seed(0)
+    x = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    for blk in x.chunk(16):
+        blk.copy_(torch.randn(blk.shape, device=DEV, generator=g))
+    w = torch.randn(N, device=DEV, generator=g)
+    out = rn.rmsnorm(x, w, eps=1e-5)
+    # first, middle and last row blocks (the last one lies beyond 2**32 elements)
+    for lo in (0, M // 2 - 64, M - 128):
+        xs = x[lo:lo + 128]
+        ref = oracle.rmsnorm_ref(xs, w, eps=1e-5, out_dtype=torch.float32)
+        assert_close_to_oracle(out[lo:lo + 128], ref, torch.bfloat16, what=f"out rows {lo}..")
+    del out, x
+
+
+def test_rmsnorm_compile_2d_then_4d():
+    """torch.compile(rmsnorm) called with a 2-D input and then, without a dynamo reset, with a 4-D
+    per-head input plus bias and residual (reference: tests/test_rmsnorm.py:168-207)."""
+    torch._dynamo.reset()
+    f = torch.compile(rn.rmsnorm, fullgraph=True)
+    x = torch.randn(32, 256, device=DEV, dtype=torch.bfloat16, requires_grad=True)
+    w = torch.randn(256, device=DEV, requires_grad=True)
+    out = f(x, w, eps=1e-5)
+    out.sum().backward()
+    ref = oracle.rmsnorm_ref(x.detach().cpu(), w.detach().cpu(), eps=1e-5, out_dtype=torch.float32)
+    assert_close_to_oracle(out.detach(), ref, torch.bfloat16, what="out 2d")
+    rstd = oracle.rmsnorm_rstd_ref(x.detach().cpu(), eps=1e-5)
+    dx_ref, _, _ = oracle.rmsnorm_bwd_ref(x.detach().cpu(), w.detach().cpu(), torch.ones(32, 256), rstd)
+    assert_close_to_oracle(x.grad, dx_ref, torch.bfloat16, max_ulp=None, what="dx 2d")
+
+    x4 = torch.randn(2, 16, 4, 64, device=DEV, dtype=torch.bfloat16, requires_grad=True)
+    w2 = torch.randn(4, 64, device=DEV, requires_grad=True)
+    b2 = torch.randn(4, 64, device=DEV, requires_grad=True)
+    r4 = torch.randn(2, 16, 4, 64, device=DEV, dtype=torch.bfloat16, requires_grad=True)
+    out2 = f(x4, w2, bias=b2, residual=r4, eps=1e-6)
+    out2.sum().backward()
+    # per-head oracle: head h of every token uses row h of the (4, 64) parameters
+    xr, rr = x4.detach().cpu().float().requires_grad_(), r4.detach().cpu().float().requires_grad_()
+    wr, br = w2.detach().cpu().clone().requires_grad_(), b2.detach().cpu().clone().requires_grad_()
+    h = xr.bfloat16().float() + rr.bfloat16().float()
+    o_ref = h * torch.rsqrt(h.square().mean(-1, keepdim=True) + 1e-6) * wr + br
+    o_ref.sum().backward()
+    assert_close_to_oracle(out2.detach(), o_ref.detach(), torch.bfloat16, what="out 4d")
+    torch.testing.assert_close(x4.grad.float().cpu(), xr.grad, atol=1e-1, rtol=1e-2)
+    torch.testing.assert_close(r4.grad.float().cpu(), rr.grad, atol=1e-1, rtol=1e-2)
+    torch.testing.assert_close(w2.grad.cpu(), wr.grad, atol=2e-2 * 32 ** 0.5, rtol=1e-2)
+    torch.testing.assert_close(b2.grad.cpu(), br.grad, atol=2e-2 * 32 ** 0.5, rtol=1e-2)
