@@ -50,7 +50,8 @@ class RmsNormBwdConfig:
                                   arch_major: Optional[int] = None, T_hint: int = 0,
                                   num_acc: int = 1) -> "RmsNormBwdConfig":
         vec = 128 // max(dtype_width, dout_width or dtype_width)
-        threads, tpr, cluster_n = _plan(N, vec, pref_elems=8192 if vec == 8 else 4096,
+        wide = 16384 if vec == 8 else 8192
+        threads, tpr, cluster_n = _plan(N, vec, pref_elems=wide if N <= 2 * wide else wide // 2,
                                         k_target=8, caps=(64 if vec == 8 else 32, 16, 8),
                                         default_threads=128)
         return cls(num_threads=threads, threads_per_row=tpr, cluster_n=cluster_n)
@@ -118,13 +119,13 @@ def get_sm_count(N: int, device, dtype: Optional[torch.dtype] = None) -> int:
     default, i.e. the first dimension of ``dw_partial`` (reference: quack/rmsnorm_config.py:265-293).
 
     Pure Python on purpose: it runs inside ``torch.compile`` traces.  Any positive value is
-    functionally valid; this one gives one persistent CTA (or two, for short rows whose ring
-    leaves room) per SM, divided by the cluster size for rows split over a cluster."""
+    functionally valid; this one gives one persistent CTA (two of 128 threads) per SM, divided
+    by the cluster size for rows split over a cluster."""
     props = torch.cuda.get_device_properties(device)
     sms = props.multi_processor_count
     width = 32 if dtype == torch.float32 else 16
     cfg = RmsNormBwdConfig.from_analytical_heuristic(N, width)
-    per_sm = 2 if cfg.num_threads <= 256 else 1
+    per_sm = 2 if cfg.num_threads <= 128 else 1  # 250+ registers per thread: 256 threads fill an SM
     return max(1, (sms * per_sm) // cfg.cluster_n)
 
 
