@@ -1,6 +1,6 @@
 """Benchmark of the row-reduction hot path on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-suite]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-suite] [--no-e2e]
 
 A step is one pass of the headline workload -- RMSNorm forward + backward, bf16 [32768, 8192] with
 a residual (weight bf16, eps 1e-6) -- on every rank (weak scaling: each GPU owns its own 32768
@@ -464,92 +464,94 @@ def run_ours(args) -> None:
     kms = tl.mean_ms()
     launches = tl.count() - (len(tl.spans.get("dw_allreduce", [])))
 
-    # ---- end to end through the public API with host buffers (rank-local, then max over ranks) ----
-    quack_rmsnorm = rn.rmsnorm
-    hx, hres, hdout = (t.cpu().pin_memory() for t in (x, res, dout))
-    hw = w.cpu().pin_memory()
-    h_out, h_dx = (torch.empty(M, N, dtype=bf).pin_memory() for _ in range(2))
-    h_dw = torch.empty(N, dtype=bf).pin_memory()
-    dxg, dresg, dwg = (torch.empty_like(x), torch.empty_like(x), torch.empty_like(w))
+    e2e = None
+    if not args.no_e2e:
+        # ---- end to end through the public API with host buffers (rank-local, then max over ranks) ----
+        quack_rmsnorm = rn.rmsnorm
+        hx, hres, hdout = (t.cpu().pin_memory() for t in (x, res, dout))
+        hw = w.cpu().pin_memory()
+        h_out, h_dx = (torch.empty(M, N, dtype=bf).pin_memory() for _ in range(2))
+        h_dw = torch.empty(N, dtype=bf).pin_memory()
+        dxg, dresg, dwg = (torch.empty_like(x), torch.empty_like(x), torch.empty_like(w))
 
-    # The user-level loop: row blocks travel host -> device on one stream, go through
-    # quack.rmsnorm + autograd backward on a second, and the results return on a third, so that
-    # the two PCIe directions and the kernels overlap.  The weight gradient accumulates in
-    # weight.grad over the blocks, as autograd does for any micro-batched loop.
-    E2E_BLOCKS = 8
-    rows_blk = M // E2E_BLOCKS
-    s_in, s_cmp, s_out = (torch.cuda.Stream(device=dev) for _ in range(3))
+        # The user-level loop: row blocks travel host -> device on one stream, go through
+        # quack.rmsnorm + autograd backward on a second, and the results return on a third, so that
+        # the two PCIe directions and the kernels overlap.  The weight gradient accumulates in
+        # weight.grad over the blocks, as autograd does for any micro-batched loop.
+        E2E_BLOCKS = 8
+        rows_blk = M // E2E_BLOCKS
+        s_in, s_cmp, s_out = (torch.cuda.Stream(device=dev) for _ in range(3))
 
-    def e2e_step():
-        cur = torch.cuda.current_stream(dev)
-        for s in (s_in, s_cmp, s_out):
-            s.wait_stream(cur)
-        with torch.cuda.stream(s_in):
-            wd = dwg.copy_(hw, non_blocking=True)
-        wd.requires_grad_()
-        ev_in = []
-        for b in range(E2E_BLOCKS):
-            sl = slice(b * rows_blk, (b + 1) * rows_blk)
+        def e2e_step():
+            cur = torch.cuda.current_stream(dev)
+            for s in (s_in, s_cmp, s_out):
+                s.wait_stream(cur)
             with torch.cuda.stream(s_in):
-                dxg[sl].copy_(hx[sl], non_blocking=True)
-                dresg[sl].copy_(hres[sl], non_blocking=True)
-                dout[sl].copy_(hdout[sl], non_blocking=True)
-                ev = torch.cuda.Event()
-                ev.record(s_in)
-                ev_in.append(ev)
-        for b in range(E2E_BLOCKS):
-            sl = slice(b * rows_blk, (b + 1) * rows_blk)
+                wd = dwg.copy_(hw, non_blocking=True)
+            wd.requires_grad_()
+            ev_in = []
+            for b in range(E2E_BLOCKS):
+                sl = slice(b * rows_blk, (b + 1) * rows_blk)
+                with torch.cuda.stream(s_in):
+                    dxg[sl].copy_(hx[sl], non_blocking=True)
+                    dresg[sl].copy_(hres[sl], non_blocking=True)
+                    dout[sl].copy_(hdout[sl], non_blocking=True)
+                    ev = torch.cuda.Event()
+                    ev.record(s_in)
+                    ev_in.append(ev)
+            for b in range(E2E_BLOCKS):
+                sl = slice(b * rows_blk, (b + 1) * rows_blk)
+                with torch.cuda.stream(s_cmp):
+                    s_cmp.wait_event(ev_in[b])
+                    xb = dxg[sl].detach().requires_grad_()
+                    rb = dresg[sl].detach().requires_grad_()
+                    o = quack_rmsnorm(xb, wd, residual=rb, eps=EPS)
+                    o.backward(dout[sl])
+                    ev = torch.cuda.Event()
+                    ev.record(s_cmp)
+                with torch.cuda.stream(s_out):
+                    s_out.wait_event(ev)
+                    o.record_stream(s_out)
+                    xb.grad.record_stream(s_out)
+                    h_out[sl].copy_(o.detach(), non_blocking=True)
+                    h_dx[sl].copy_(xb.grad, non_blocking=True)  # dresidual is the same tensor
             with torch.cuda.stream(s_cmp):
-                s_cmp.wait_event(ev_in[b])
-                xb = dxg[sl].detach().requires_grad_()
-                rb = dresg[sl].detach().requires_grad_()
-                o = quack_rmsnorm(xb, wd, residual=rb, eps=EPS)
-                o.backward(dout[sl])
+                dwv = wd.grad
+                if world > 1:
+                    d32 = dwv.float()
+                    dist.all_reduce(d32)
+                    dwv = d32.to(bf)
+                dwv.record_stream(s_out)
                 ev = torch.cuda.Event()
                 ev.record(s_cmp)
             with torch.cuda.stream(s_out):
                 s_out.wait_event(ev)
-                o.record_stream(s_out)
-                xb.grad.record_stream(s_out)
-                h_out[sl].copy_(o.detach(), non_blocking=True)
-                h_dx[sl].copy_(xb.grad, non_blocking=True)  # dresidual is the same tensor
-        with torch.cuda.stream(s_cmp):
-            dwv = wd.grad
-            if world > 1:
-                d32 = dwv.float()
-                dist.all_reduce(d32)
-                dwv = d32.to(bf)
-            dwv.record_stream(s_out)
-            ev = torch.cuda.Event()
-            ev.record(s_cmp)
-        with torch.cuda.stream(s_out):
-            s_out.wait_event(ev)
-            h_dw.copy_(dwv, non_blocking=True)
-        for s in (s_in, s_cmp, s_out):
-            cur.wait_stream(s)
-        dwg.grad = None
-        dwg.requires_grad_(False)
+                h_dw.copy_(dwv, non_blocking=True)
+            for s in (s_in, s_cmp, s_out):
+                cur.wait_stream(s)
+            dwg.grad = None
+            dwg.requires_grad_(False)
 
-    e2e_steps = max(3, min(args.steps, 5))
-    for _ in range(2):
-        e2e_step()
-    sync_all()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(e2e_steps):
-        e2e_step()
-    e1.record()
-    sync_all()
-    e2e_ms = torch.tensor([e0.elapsed_time(e1) / e2e_steps], device=dev)
-    if world > 1:
-        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-    e2e = {"value": world * step_bytes / float(e2e_ms) / 1e6, "unit": "GB/s",
-           "h2d_bytes_per_step": 3 * M * N * 2 + N * 2, "d2h_bytes_per_step": 2 * M * N * 2 + N * 2,
-           "ms_per_step": float(e2e_ms),
-           "api": "quack.rmsnorm(x, w, residual=res) + backward through autograd on 8 row blocks; "
-                  "pinned host buffers; x, residual, dout, weight copied in on one stream, out, "
-                  "dx (= dresidual), dw copied back on another, kernels on a third"}
-    del hx, hres, hdout, h_out, h_dx
+        e2e_steps = max(3, min(args.steps, 5))
+        for _ in range(2):
+            e2e_step()
+        sync_all()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(e2e_steps):
+            e2e_step()
+        e1.record()
+        sync_all()
+        e2e_ms = torch.tensor([e0.elapsed_time(e1) / e2e_steps], device=dev)
+        if world > 1:
+            dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+        e2e = {"value": world * step_bytes / float(e2e_ms) / 1e6, "unit": "GB/s",
+               "h2d_bytes_per_step": 3 * M * N * 2 + N * 2, "d2h_bytes_per_step": 2 * M * N * 2 + N * 2,
+               "ms_per_step": float(e2e_ms),
+               "api": "quack.rmsnorm(x, w, residual=res) + backward through autograd on 8 row blocks; "
+                      "pinned host buffers; x, residual, dout, weight copied in on one stream, out, "
+                      "dx (= dresidual), dw copied back on another, kernels on a third"}
+        del hx, hres, hdout, h_out, h_dx
 
     if rank == 0:
         fwd_ms = kms["rmsnorm_fwd"]
@@ -609,6 +611,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-suite", action="store_true", help="skip the per-kernel sweep of the other configurations")
+    ap.add_argument("--no-e2e", action="store_true",
+                    help="skip the end-to-end leg (for profiler launch lists of the timed step alone)")
     ap.add_argument("--only", default=None, help="run one kernel on a small case (for ncu captures)")
     ap.add_argument("--rows", type=int, default=0)
     ap.add_argument("--cols", type=int, default=0)
