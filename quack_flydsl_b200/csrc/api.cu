@@ -88,6 +88,51 @@ int cached_occupancy(const void* kernel, int threads, size_t smem) {
   return occ;
 }
 
+int cached_max_clusters(const void* kernel, int threads, size_t smem, int cluster_n) {
+  struct Key {
+    const void* k; int t; size_t s; int c; int dev;
+    bool operator<(const Key& o) const {
+      if (k != o.k) return k < o.k;
+      if (t != o.t) return t < o.t;
+      if (s != o.s) return s < o.s;
+      if (c != o.c) return c < o.c;
+      return dev < o.dev;
+    }
+  };
+  static std::map<Key, int> cache;
+  static std::mutex mu;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const Key key{kernel, threads, smem, cluster_n, dev};
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  if (smem > 32 * 1024)
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (cluster_n > 8) cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(cluster_n), 1, 1);
+  cfg.blockDim = dim3(static_cast<unsigned>(threads), 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(cluster_n);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess || n < 1) {
+    cudaGetLastError();
+    n = 0;  // unknown: the caller falls back to resident CTAs / cluster size
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  cache[key] = n;
+  return n;
+}
+
 const DeviceFacts* current_device_facts() {
   int device = -1;
   cudaError_t e = cudaGetDevice(&device);

@@ -198,6 +198,21 @@ inline int plan_rows(const char* op, int64_t N, int vec, const ElemCaps& caps,
 // launch shape).  Persistent kernels use exactly this many CTAs: more would run as a second,
 // partially filled wave.
 int cached_occupancy(const void* kernel, int threads, size_t smem);
+// Clusters of `cluster_n` CTAs of `kernel` that are resident on the device at once (cached).  A
+// cluster must fit inside one GPC, so this is less than resident CTAs / cluster_n: on B200 with
+// two 128-thread CTAs per SM, 32 clusters of 8 and 15 clusters of 16.  0 if the query fails.
+int cached_max_clusters(const void* kernel, int threads, size_t smem, int cluster_n);
+template <class Params>
+int resident_clusters(void (*kernel)(Params), int threads, size_t smem, int cluster_n, int sm_count) {
+  if (cluster_n > 1) {
+    const int n = cached_max_clusters(reinterpret_cast<const void*>(kernel), threads, smem, cluster_n);
+    if (n > 0) return n;
+  }
+  int per_sm = cached_occupancy(reinterpret_cast<const void*>(kernel), threads, smem);
+  if (per_sm < 1) per_sm = 1;
+  const int n = per_sm * sm_count / cluster_n;
+  return n > 0 ? n : 1;
+}
 template <class Params>
 int resident_ctas(void (*kernel)(Params), int threads, size_t smem, int sm_count) {
   int per_sm = cached_occupancy(reinterpret_cast<const void*>(kernel), threads, smem);
@@ -254,8 +269,8 @@ template <class Params>
 int launch_persistent(void (*kernel)(Params), int64_t num_tiles, int grid_y, int threads,
                       size_t smem, int cluster_n, int max_ctas, int sm_count, cudaStream_t stream,
                       const Params& params, const char* name) {
-  int64_t cap = max_ctas > 0 ? max_ctas : resident_ctas(kernel, threads, smem, sm_count);
-  cap /= cluster_n;
+  int64_t cap = max_ctas > 0 ? max_ctas / cluster_n
+                             : resident_clusters(kernel, threads, smem, cluster_n, sm_count);
   if (grid_y > 1 && max_ctas <= 0) cap = (cap + grid_y - 1) / grid_y;
   if (cap < 1) cap = 1;
   int64_t clusters = num_tiles < cap ? num_tiles : cap;

@@ -456,8 +456,18 @@ static int default_num_partials(const NormBwdPlan& plan, const DeviceFacts* dev)
   const int by_smem = static_cast<int>(smem_per_sm / (plan.smem + 2048));
   if (per_sm > by_smem) per_sm = by_smem;
   if (per_sm < 1) per_sm = 1;
-  if (per_sm > 2) per_sm = 2;
   int clusters = dev->sm_count * per_sm / plan.rows.cluster_n;
+  if (plan.rows.cluster_n > 1) {
+    // A cluster has to fit into one GPC, so fewer clusters are resident than CTAs / cluster size
+    // (B200: 32 clusters of 8, 15 of 16 at two CTAs per SM).  One cluster too many runs as a
+    // second wave and nearly doubles the time, so ask the occupancy calculator.  All stage-1
+    // instantiations have the same footprint class; the plainest one stands for them.
+    const void* rep = plan.rows.vec == 4
+                          ? reinterpret_cast<const void*>(norm_bwd_kernel<QB_F32, 4, 8, false, false, 0>)
+                          : reinterpret_cast<const void*>(norm_bwd_kernel<QB_BF16, 8, 8, false, false, 0>);
+    const int n = cached_max_clusters(rep, plan.rows.threads, plan.smem, plan.rows.cluster_n);
+    if (n > 0 && n < clusters) clusters = n;
+  }
   if (clusters < 1) clusters = 1;
   return clusters;
 }

@@ -114,19 +114,38 @@ def _plan(N: int, vec: int, pref_elems: int, k_target: int, caps, default_thread
     return threads, tpr, cluster_n
 
 
+# Clusters that are resident at once on B200 (a cluster has to fit into one GPC), by cluster size,
+# for the backward kernel's two CTAs of 128 threads per SM; used when the library cannot be asked.
+_B200_RESIDENT_CLUSTERS = {4: 64, 8: 32, 16: 15}  # 8 and 16 measured, 4 estimated
+
+
 def get_sm_count(N: int, device, dtype: Optional[torch.dtype] = None) -> int:
     """Number of partial-sum slices (persistent CTAs or clusters) the backward kernel uses by
     default, i.e. the first dimension of ``dw_partial`` (reference: quack/rmsnorm_config.py:265-293).
 
-    Pure Python on purpose: it runs inside ``torch.compile`` traces.  Any positive value is
-    functionally valid; this one gives one persistent CTA (two of 128 threads) per SM, divided
-    by the cluster size for rows split over a cluster."""
+    Any positive value is functionally valid.  Eagerly the library is asked
+    (``qb_norm_bwd_num_partials``: one persistent CTA -- two of 128 threads -- per SM, or as many
+    clusters as are resident at once); inside ``torch.compile`` traces a pure-Python estimate of
+    the same number is returned."""
     props = torch.cuda.get_device_properties(device)
     sms = props.multi_processor_count
     width = 32 if dtype == torch.float32 else 16
+    if not torch.compiler.is_compiling():
+        from quack_flydsl_b200 import _C
+
+        code = _C.FLOAT_CODES[torch.float32 if width == 32 else torch.bfloat16]
+        with torch.cuda.device(device):
+            n = _C.lib().qb_norm_bwd_num_partials(int(N), code, 0, -1)
+        if n > 0:
+            return int(n)
     cfg = RmsNormBwdConfig.from_analytical_heuristic(N, width)
     per_sm = 2 if cfg.num_threads <= 128 else 1  # 250+ registers per thread: 256 threads fill an SM
-    return max(1, (sms * per_sm) // cfg.cluster_n)
+    n = (sms * per_sm) // cfg.cluster_n
+    if cfg.cluster_n > 2 and per_sm == 2:
+        n = min(n, _B200_RESIDENT_CLUSTERS.get(cfg.cluster_n, n))
+    elif cfg.cluster_n > 2:
+        n = min(n, _B200_RESIDENT_CLUSTERS.get(cfg.cluster_n, n) // 2)
+    return max(1, n)
 
 
 _CTA_THREAD_SIZE = (128, 256, 512)
