@@ -387,8 +387,20 @@ extern "C" int qb_norm_fwd(const qb_norm_fwd_args* args, qb_stream_t stream) {
   // forces it for any row, flag bit 1 disables it.
   const int64_t row_bytes = a.N * host_dtype_bytes(a.x_dtype);
   const bool long_row = row_bytes >= (a.residual != nullptr ? (128 << 10) : (64 << 10));
+  // The streamed kernel writes residual_out in its first pass and reads x / residual again in the
+  // second one, so residual_out must not overlap either input (the register kernels allow that).
+  auto overlaps = [&](const void* in, int64_t in_stride) {
+    if (a.residual_out == nullptr || in == nullptr) return false;
+    const int eb = host_dtype_bytes(a.x_dtype);
+    const char* o0 = static_cast<const char*>(a.residual_out);
+    const char* o1 = o0 + ((a.M - 1) * a.residual_out_row_stride + a.N) * eb;
+    const char* i0 = static_cast<const char*>(in);
+    const char* i1 = i0 + ((a.M - 1) * in_stride + a.N) * eb;
+    return o0 < i1 && i0 < o1;
+  };
+  const bool aliased = overlaps(a.x, a.x_row_stride) || overlaps(a.residual, a.residual_row_stride);
   if (uniform && a.H == 1 && a.cfg.cluster_n == 0 && !(a.cfg.flags & 2) && a.M >= dev->sm_count &&
-      (long_row || (a.cfg.flags & 16))) {
+      !aliased && (long_row || (a.cfg.flags & 16))) {
     const int t = a.cfg.num_threads > 0 ? a.cfg.num_threads : (a.residual != nullptr ? 512 : 256);
     p.tpr = t;
     p.rows_per_cta = 1;

@@ -1,8 +1,8 @@
 """Generates tests/golden/*.pt: inputs and outputs of the reference's own CPU-runnable code.
 
-Run in a container where the reference tree is mounted (default /root/reference):
+Run where a checkout of the reference project is available:
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <path to the reference tree>
 
 What is executed:
 * ``rmsnorm_ref``, ``rmsnorm_bwd_ref``, ``layernorm_ref``, ``layernorm_rstd_ref``,
@@ -183,7 +183,7 @@ def gen_linear_ce(ref_root: Path) -> dict:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="root of the reference project checkout")
     args = ap.parse_args()
     torch.manual_seed(0)
     torch.set_num_threads(1)  # fixed summation order in the generating run

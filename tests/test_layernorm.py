@@ -203,3 +203,20 @@ def test_norm_forward_streamed_long_rows(force, monkeypatch):
     torch.testing.assert_close(mn.cpu(), oracle.layernorm_mean_ref(x.cpu()), atol=0, rtol=1e-6)
     torch.testing.assert_close(rs.cpu(), oracle.layernorm_rstd_ref(x.cpu(), eps=1e-5), atol=0, rtol=2e-4)
     torch.testing.assert_close(o.cpu(), oracle.layernorm_ref(x.cpu(), w.cpu(), eps=1e-5), atol=5e-3, rtol=1e-3)
+
+
+def test_norm_forward_long_rows_residual_out_in_place():
+    """residual_out may be the residual buffer itself (in-place residual stream update); long rows
+    must then not take the kernel that reads the inputs a second time."""
+    M, N = 160, 65536
+    g = torch.Generator(device=DEV).manual_seed(11)
+    x = torch.randn(M, N, device=DEV, generator=g).bfloat16()
+    res = torch.randn(M, N, device=DEV, generator=g).bfloat16()
+    w = (1 + 0.1 * torch.randn(N, device=DEV, generator=g)).bfloat16()
+    ref_out, ref_h = oracle.rmsnorm_ref(x.cpu(), w.cpu(), residual=res.cpu(), out_dtype=torch.float32,
+                                        residual_dtype=torch.float32)
+    out = torch.empty_like(x)
+    rstd = torch.empty(M, device=DEV)
+    rnm._rmsnorm_fwd(x, w, out, None, rstd, None, res, res, 1e-6)  # residual_out is residual
+    assert torch.equal(res.cpu(), ref_h.bfloat16())
+    assert_close_to_oracle(out, ref_out, torch.bfloat16, what="out")
