@@ -114,9 +114,11 @@ def _plan(N: int, vec: int, pref_elems: int, k_target: int, caps, default_thread
     return threads, tpr, cluster_n
 
 
-# Clusters that are resident at once on B200 (a cluster has to fit into one GPC), by cluster size,
-# for the backward kernel's two CTAs of 128 threads per SM; used when the library cannot be asked.
-_B200_RESIDENT_CLUSTERS = {4: 64, 8: 32, 16: 15}  # 8 and 16 measured, 4 estimated
+# What qb_norm_bwd_num_partials returns on B200 (148 SMs) by row length in units of 16-byte
+# chunks: two 128-thread CTAs per SM, one 256-thread CTA per SM, clusters of 2 such CTAs, then the
+# resident clusters of 8 / 16 CTAs of 128 threads and of 16 CTAs of 256 threads (a cluster has to
+# fit into one GPC, which is why these are not 296 / cluster size).
+_B200_PARTIALS_BY_CHUNKS = ((1024, 296), (2048, 148), (4096, 74), (8192, 32), (16384, 15))
 
 
 def get_sm_count(N: int, device, dtype: Optional[torch.dtype] = None) -> int:
@@ -138,14 +140,13 @@ def get_sm_count(N: int, device, dtype: Optional[torch.dtype] = None) -> int:
             n = _C.lib().qb_norm_bwd_num_partials(int(N), code, 0, -1)
         if n > 0:
             return int(n)
-    cfg = RmsNormBwdConfig.from_analytical_heuristic(N, width)
-    per_sm = 2 if cfg.num_threads <= 128 else 1  # 250+ registers per thread: 256 threads fill an SM
-    n = (sms * per_sm) // cfg.cluster_n
-    if cfg.cluster_n > 2 and per_sm == 2:
-        n = min(n, _B200_RESIDENT_CLUSTERS.get(cfg.cluster_n, n))
-    elif cfg.cluster_n > 2:
-        n = min(n, _B200_RESIDENT_CLUSTERS.get(cfg.cluster_n, n) // 2)
-    return max(1, n)
+    chunks = -(-int(N) * width // 128)
+    per_148 = 7
+    for limit, count in _B200_PARTIALS_BY_CHUNKS:
+        if chunks <= limit:
+            per_148 = count
+            break
+    return max(1, per_148 * sms // 148)
 
 
 _CTA_THREAD_SIZE = (128, 256, 512)

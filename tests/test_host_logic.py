@@ -156,3 +156,24 @@ def test_row_stride_helper():
     assert rn_mod._row_stride(y) == 64
     assert rn_mod._row_stride(y[:, :3]) is None  # (4, 3, 64) view: rows not uniformly strided
     assert rn_mod._row_stride(torch.empty(8, 64).t()) is None
+
+
+def test_get_sm_count_pure_python_estimate(monkeypatch):
+    """Inside torch.compile traces get_sm_count cannot ask the library; the pure-Python estimate
+    gives one persistent CTA (two of 128 threads) per SM, or the clusters resident at once."""
+    import types
+
+    from quack_flydsl_b200 import rmsnorm_config as rc
+
+    monkeypatch.setattr(torch.cuda, "get_device_properties",
+                        lambda device: types.SimpleNamespace(multi_processor_count=148))
+    monkeypatch.setattr(torch.compiler, "is_compiling", lambda: True)
+    assert rc.get_sm_count(4096, "cuda", torch.bfloat16) == 296     # 128-thread CTAs, two per SM
+    assert rc.get_sm_count(8192, "cuda", torch.bfloat16) == 296
+    assert rc.get_sm_count(16384, "cuda", torch.bfloat16) == 148    # one 256-thread CTA per SM
+    assert rc.get_sm_count(32768, "cuda", torch.bfloat16) == 74     # clusters of two such CTAs
+    assert rc.get_sm_count(65536, "cuda", torch.bfloat16) == 32     # clusters of 8
+    assert rc.get_sm_count(131072, "cuda", torch.bfloat16) == 15    # clusters of 16
+    assert rc.get_sm_count(262144, "cuda", torch.bfloat16) == 7    # clusters of 16 CTAs of 256 threads
+    assert rc.get_sm_count(8192, "cuda", torch.float32) == 148
+    assert rc.get_sm_count(4096, "cuda", torch.float32) == 296
