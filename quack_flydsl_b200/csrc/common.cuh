@@ -731,20 +731,23 @@ __device__ __forceinline__ float2 shfl_xor_f2(float2 v, int mask) {
 // Reduces `v` over all threads that share a row (and over the cluster's CTAs).  Every thread of
 // the row returns the same value.  Must be called by all threads of the CTA (and, with clusters,
 // by all CTAs of the cluster) the same number of times with the same (stage, parity).
-// Barrier among the threads that share a row.  When a CTA carries several rows, each row group
-// (whole warps) synchronises on a hardware barrier of its own (ids 1 ... 15) instead of stalling
-// on the other groups at the CTA-wide barrier 0.
+// Barrier among the threads that share a row.  ROWBAR: when a CTA carries several rows, each row
+// group (whole warps) synchronises on a hardware barrier of its own (ids 1 ... 15) instead of
+// the CTA-wide barrier 0.  Measured on B200: LayerNorm forward N = 8192 (4 rows of 2 warps per
+// CTA) +15 %, but softmax backward N = 4096 -23 % and LayerNorm backward -6 %, so it is opt-in
+// per kernel.
+template <bool ROWBAR>
 __device__ __forceinline__ void row_group_sync(const RowGeom& g) {
-#ifndef QB_NO_ROW_BARRIERS
-  if (g.tpr >= 32 && g.tpr < static_cast<int>(blockDim.x) && g.r < 15) {
-    asm volatile("bar.sync %0, %1;" ::"r"(g.r + 1), "r"(g.tpr) : "memory");
-    return;
+  if constexpr (ROWBAR) {
+    if (g.tpr >= 32 && g.tpr < static_cast<int>(blockDim.x) && g.r < 15) {
+      asm volatile("bar.sync %0, %1;" ::"r"(g.r + 1), "r"(g.tpr) : "memory");
+      return;
+    }
   }
-#endif
   __syncthreads();
 }
 
-template <class Op>
+template <class Op, bool ROWBAR = false>
 __device__ __forceinline__ float2 row_reduce(float2 v, const RowGeom& g, ReduceScratch& s,
                                              int stage, int parity) {
   // 1. within the warp (or the sub-warp row group)
@@ -776,7 +779,7 @@ __device__ __forceinline__ float2 row_reduce(float2 v, const RowGeom& g, ReduceS
   if (g.warps_per_row > 1) {
     float2* buf = s.warp_part[stage][parity];
     if (g.lane == 0) buf[g.warp_base + g.warp_in_row] = v;
-    row_group_sync(g);
+    row_group_sync<ROWBAR>(g);
     v = g.lane < g.warps_per_row ? buf[g.warp_base + g.lane] : Op::identity();
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v = Op::combine(v, shfl_xor_f2(v, o));

@@ -173,7 +173,7 @@ norm_fwd_kernel(const NormFwdParams p) {
           vadd<VEC>(sv, sv, v[k]);
         }
       }
-      mean = row_reduce<SumOp>(make_float2(hsum<VEC>(sv), 0.f), g, scratch, 0, parity).x * inv_n;
+      mean = row_reduce<SumOp, true>(make_float2(hsum<VEC>(sv), 0.f), g, scratch, 0, parity).x * inv_n;
       // sum (x - mean)^2; padding chunks hold zeros and get offset 0 instead of -mean
       float qv[VEC];
 #pragma unroll
@@ -193,7 +193,7 @@ norm_fwd_kernel(const NormFwdParams p) {
         vfma<VEC>(qv, d, d, qv);
       }
       const float var =
-          row_reduce<SumOp>(make_float2(hsum<VEC>(qv), 0.f), g, scratch, 1, parity).x * inv_n;
+          row_reduce<SumOp, true>(make_float2(hsum<VEC>(qv), 0.f), g, scratch, 1, parity).x * inv_n;
       rstd = rsqrtf(var + a.eps);
     } else {
       float qv[VEC];
@@ -210,7 +210,7 @@ norm_fwd_kernel(const NormFwdParams p) {
         }
       }
       const float ms =
-          row_reduce<SumOp>(make_float2(hsum<VEC>(qv), 0.f), g, scratch, 0, parity).x * inv_n;
+          row_reduce<SumOp, true>(make_float2(hsum<VEC>(qv), 0.f), g, scratch, 0, parity).x * inv_n;
       rstd = rsqrtf(ms + a.eps);
     }
     parity ^= 1;
