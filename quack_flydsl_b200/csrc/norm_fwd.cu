@@ -22,7 +22,7 @@ namespace qb {
 // DT: dtype shared by x / residual / out / residual_out, or kDynDT (per-tensor run-time dtypes).
 // VEC: elements per chunk; K: chunks per thread; LN: LayerNorm instead of RMSNorm;
 // RAW: keep the packed input words instead of fp32 values (no residual, static 16-bit DT only).
-template <int DT, int VEC, int K, bool LN, bool RAW, bool STAGED>
+template <int DT, int VEC, int K, bool LN, bool RAW, int STAGED>
 __global__ void __launch_bounds__(RAW ? (K * VEC > 32 ? 256 : (K * VEC > 16 ? 512 : 1024))
                                       : (K * VEC > 32 ? 256 : (K * VEC > 16 ? 512 : 1024)),
                                   (K * VEC > 32) ? 2 : 1)
@@ -60,7 +60,8 @@ norm_fwd_kernel(const NormFwdParams p) {
   // occupancy are read from global memory (L1/L2) instead.
   const bool has_w = a.weight != nullptr;
   const bool has_b = a.bias != nullptr;
-  constexpr bool staged = STAGED;
+  constexpr bool staged = STAGED != 0;
+  constexpr bool packed_params = STAGED == 2;  // staged in their own 16-bit dtype, 16 bytes per chunk
   const int64_t wrow = static_cast<int64_t>(h) * N;
   // Slots exist for all tpr * K chunk positions of the tile geometry (the epilogue reads the
   // slots of padding chunks too, it only does not store their results).
@@ -85,7 +86,24 @@ norm_fwd_kernel(const NormFwdParams p) {
   };
   float* w_smem = reinterpret_cast<float*>(smem_params);
   float* b_smem = w_smem + static_cast<size_t>(slice_chunks) * VEC;
-  if constexpr (staged) {
+  if constexpr (packed_params) {
+    // weight and bias share one 16-bit dtype: copy the chunks as they are (slot c = 16 bytes)
+    static_assert(!packed_params || VEC == 8, "packed parameter staging uses 8-element chunks");
+    uint4* w16 = reinterpret_cast<uint4*>(smem_params);
+    uint4* b16 = w16 + slice_chunks;
+    for (int c = threadIdx.x; c < nchunks; c += nthreads) {
+      uint32_t raw[4];
+      if (has_w) {
+        ldg_cached<16>(raw, reinterpret_cast<const char*>(a.weight) + (wrow + col0 + c * VEC) * 2);
+        w16[c] = make_uint4(raw[0], raw[1], raw[2], raw[3]);
+      }
+      if (has_b) {
+        ldg_cached<16>(raw, reinterpret_cast<const char*>(a.bias) + (wrow + col0 + c * VEC) * 2);
+        b16[c] = make_uint4(raw[0], raw[1], raw[2], raw[3]);
+      }
+    }
+    __syncthreads();
+  } else if constexpr (staged) {
     for (int c = threadIdx.x; c < nchunks; c += nthreads) {
       float pv[VEC];
       if (has_w) load_chunk<kDynDT, VEC, false>(pv, a.weight, wrow + col0 + c * VEC, a.weight_dtype);
@@ -227,12 +245,34 @@ norm_fwd_kernel(const NormFwdParams p) {
 #pragma unroll
       for (int k = 0; k < K; ++k) {
         float w[VEC], b[VEC], y[VEC], xc[VEC];
-        load_param(w, w_smem, chunk0 + k * p.tpr);
-        if (has_b) {
-          load_param(b, b_smem, chunk0 + k * p.tpr);
-        } else {
+        if constexpr (packed_params) {
+          const uint4* w16 = reinterpret_cast<const uint4*>(smem_params);
+          const uint4* b16 = w16 + slice_chunks;
+          const bool pbf16 = (has_w ? a.weight_dtype : a.bias_dtype) == QB_BF16;
+          uint32_t raw[4];
+          if (has_w) {
+            lds_raw<16>(raw, w16 + chunk0 + k * p.tpr);
+            unpack16<VEC>(w, raw, pbf16);
+            vadd_s<VEC>(w, w, a.weight_offset);
+          } else {
 #pragma unroll
-          for (int i = 0; i < VEC; ++i) b[i] = 0.0f;
+            for (int i = 0; i < VEC; ++i) w[i] = 1.0f;
+          }
+          if (has_b) {
+            lds_raw<16>(raw, b16 + chunk0 + k * p.tpr);
+            unpack16<VEC>(b, raw, pbf16);
+          } else {
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) b[i] = 0.0f;
+          }
+        } else {
+          load_param(w, w_smem, chunk0 + k * p.tpr);
+          if (has_b) {
+            load_param(b, b_smem, chunk0 + k * p.tpr);
+          } else {
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) b[i] = 0.0f;
+          }
         }
         if constexpr (RAW) {
           forget_values(rx[k]);
@@ -290,10 +330,15 @@ static int launch_norm_fwd_s(const NormFwdParams& p, FwdGrid grid, int threads, 
                              cudaStream_t st) {
   const int heads = static_cast<int>(p.a.H);
   const char* name = LN ? "layernorm_fwd" : "rmsnorm_fwd";
+  if constexpr (VEC == 8) {
+    if (p.stage_params == 2)
+      return launch_persistent(norm_fwd_kernel<DT, VEC, K, LN, RAW, 2>, p.num_tiles, heads, threads,
+                               smem, p.cluster_n, grid.max_ctas, grid.sm_count, st, p, name);
+  }
   if (p.stage_params)
-    return launch_persistent(norm_fwd_kernel<DT, VEC, K, LN, RAW, true>, p.num_tiles, heads,
+    return launch_persistent(norm_fwd_kernel<DT, VEC, K, LN, RAW, 1>, p.num_tiles, heads,
                              threads, smem, p.cluster_n, grid.max_ctas, grid.sm_count, st, p, name);
-  return launch_persistent(norm_fwd_kernel<DT, VEC, K, LN, RAW, false>, p.num_tiles, heads, threads,
+  return launch_persistent(norm_fwd_kernel<DT, VEC, K, LN, RAW, 0>, p.num_tiles, heads, threads,
                            smem, p.cluster_n, grid.max_ctas, grid.sm_count, st, p, name);
 }
 
@@ -371,7 +416,7 @@ extern "C" int qb_norm_fwd(const qb_norm_fwd_args* args, qb_stream_t stream) {
   // Packed rows: 16 chunks per thread (one warp per 4096-element row), CTAs of 256 threads from
   // 6144 elements on (measured: RMSNorm N = 8192 6.0 -> 6.5 TB/s, N = 12288 5.1 -> 6.2,
   // LayerNorm N = 6144 4.2 -> 5.0); fp32-held rows 8 chunks per thread.
-  const int k_target = (raw && !(a.is_layernorm && a.N >= 12288)) ? 16 : 8;
+  const int k_target = raw ? 16 : 8;
   if (int rc = plan_rows("norm_fwd", a.N, vec, caps, pref, k_target, raw && a.N >= 6144 ? 256 : 128,
                          a.cfg, &plan))
     return rc;
@@ -383,10 +428,12 @@ extern "C" int qb_norm_fwd(const qb_norm_fwd_args* args, qb_stream_t stream) {
   p.flags = a.cfg.flags;
   // Long rows with at least one row per SM: the streamed two-pass kernel with the row parked in
   // L2.  Measured on B200 (bf16, 1 GiB per tensor) it overtakes the register / cluster kernels
-  // from 64 KB per row (128 KB with a residual, where two tensors are streamed); flag bit 4
+  // from 64 KB per row (48 KB for LayerNorm, 128 KB with a residual, where two tensors are
+  // streamed); flag bit 4
   // forces it for any row, flag bit 1 disables it.
   const int64_t row_bytes = a.N * host_dtype_bytes(a.x_dtype);
-  const bool long_row = row_bytes >= (a.residual != nullptr ? (128 << 10) : (64 << 10));
+  const bool long_row =
+      row_bytes >= (a.residual != nullptr ? (128 << 10) : (a.is_layernorm ? (48 << 10) : (64 << 10)));
   // The streamed kernel writes residual_out in its first pass and reads x / residual again in the
   // second one, so residual_out must not overlap either input (the register kernels allow that).
   auto overlaps = [&](const void* in, int64_t in_stride) {
@@ -420,7 +467,19 @@ extern "C" int qb_norm_fwd(const qb_norm_fwd_args* args, qb_stream_t stream) {
   // small enough to leave room for several CTAs per SM.
   size_t smem = static_cast<size_t>(plan.tpr) * plan.K * vec * 4 * (a.bias ? 2 : 1);
   p.stage_params = smem <= 64 * 1024;
-  if (!p.stage_params) smem = 0;
+  if (!p.stage_params) {
+    // Too large as fp32: 16-bit weight and bias of one dtype are staged as they are (half the
+    // bytes, unpacked in the epilogue) while that fits.
+    const size_t packed = static_cast<size_t>(plan.tpr) * plan.K * 16 * (a.bias ? 2 : 1);
+    const int pdt = a.weight ? a.weight_dtype : a.bias_dtype;
+    const bool same = (a.weight == nullptr || a.bias == nullptr || a.weight_dtype == a.bias_dtype);
+    if (vec == 8 && (a.weight || a.bias) && pdt != QB_F32 && same && packed <= 64 * 1024) {
+      p.stage_params = 2;
+      smem = packed;
+    } else {
+      smem = 0;
+    }
+  }
   // Persistent grid: exactly the CTAs that are resident at once, each walking over row tiles (so
   // weight / bias are staged once per CTA, not once per row).
   const FwdGrid grid = {a.cfg.max_ctas, dev->sm_count};

@@ -220,3 +220,28 @@ def test_norm_forward_long_rows_residual_out_in_place():
     rnm._rmsnorm_fwd(x, w, out, None, rstd, None, res, res, 1e-6)  # residual_out is residual
     assert torch.equal(res.cpu(), ref_h.bfloat16())
     assert_close_to_oracle(out, ref_out, torch.bfloat16, what="out")
+
+
+@pytest.mark.parametrize("N", [12288, 16384])
+@pytest.mark.parametrize("pdtype", [torch.bfloat16, torch.float16])
+def test_norm_forward_packed_parameter_staging(N, pdtype):
+    """Rows whose fp32 weight + bias slices no longer fit the shared-memory staging keep 16-bit
+    parameters packed there; LayerNorm and RMSNorm with bias, weight_offset included."""
+    M = 200
+    dtype = pdtype
+    g = torch.Generator(device=DEV).manual_seed(7)
+    x = (0.5 + torch.randn(M, N, device=DEV, generator=g)).to(dtype)
+    w = (1 + 0.1 * torch.randn(N, device=DEV, generator=g)).to(pdtype)
+    b = (0.1 * torch.randn(N, device=DEV, generator=g)).to(pdtype)
+    xc, wc, bc = x.cpu(), w.cpu(), b.cpu()
+    o = torch.empty_like(x)
+    rs, mn = torch.empty(M, device=DEV), torch.empty(M, device=DEV)
+    rnm._rmsnorm_fwd(x, w, o, b, rs, mn, None, None, 1e-5, True)
+    assert_close_to_oracle(o, oracle.layernorm_ref(xc, wc, bc, eps=1e-5), dtype, what="ln out")
+    torch.testing.assert_close(rs.cpu(), oracle.layernorm_rstd_ref(xc, eps=1e-5), atol=0, rtol=1e-5)
+    rnm._rmsnorm_fwd(x, w, o, b, rs, None, None, None, 1e-6, False, 0.5)
+    ref = oracle.rmsnorm_ref(xc, wc, bias=bc, weight_offset=0.5, out_dtype=torch.float32)
+    assert_close_to_oracle(o, ref, dtype, what="rms out")
+    rnm._rmsnorm_fwd(x, None, o, b, rs, mn, None, None, 1e-5, True)  # bias only
+    ref = oracle.layernorm_ref(xc, torch.ones(N), bc, eps=1e-5)
+    assert_close_to_oracle(o, ref, dtype, what="ln bias-only out")
