@@ -23,7 +23,7 @@
 extern "C" {
 #endif
 
-#define QB_ABI_VERSION 1
+#define QB_ABI_VERSION 2
 
 /* element types of streamed tensors */
 enum qb_dtype { QB_F32 = 0, QB_F16 = 1, QB_BF16 = 2 };
@@ -52,13 +52,21 @@ typedef struct qb_launch_cfg {
   int32_t stages;          /* shared-memory prefetch stages (norm backward); chunks in flight per
                               thread and input (streamed softmax: 4 / 8 forward, 2 / 4 backward);
                               0 = heuristic */
-  int32_t flags;           /* measurement switches, 0 in production.
-                              bit 0: keep rows as fp32 registers even where the packed 16-bit mode applies
-                              bit 1: never use the streamed two-pass kernels for long rows
-                              bit 2 / bit 3: streamed kernels: plain L2 policy for pass 1 / pass 2
-                              bit 4: norm forward: streamed two-pass kernel for any row length */
-  int32_t reserved[2];
+  int32_t flags;           /* kernel-selection bits for tuning builds; 0 = heuristic (see the
+                              QB_FLAG_* constants below) */
+  int32_t ctas_per_sm;     /* shared-memory ring kernels: CTAs that share one SM (1 or 2); 0 = heuristic */
+  int32_t reserved;
 } qb_launch_cfg;
+
+/* qb_launch_cfg.flags: which of several equivalent kernels serves a call.  Results do not depend
+ * on them; they exist so that a tuning build can compare the alternatives. */
+#define QB_FLAG_NO_PACKED 1    /* keep rows as fp32 registers where the packed 16-bit mode applies */
+#define QB_FLAG_NO_TWO_PASS 2  /* long rows: never the two-pass kernels, always registers + clusters */
+#define QB_FLAG_L2_PLAIN_1 4   /* two-pass kernels that re-read from L2: plain L2 policy, pass 1 */
+#define QB_FLAG_L2_PLAIN_2 8   /* ... and pass 2 */
+#define QB_FLAG_FORCE_TWO_PASS 16 /* two-pass kernel for any row length */
+#define QB_FLAG_NO_RING 32     /* long rows: re-read from L2 instead of the shared-memory ring */
+#define QB_FLAG_RING_FWD 64    /* softmax forward, long rows: the shared-memory ring kernel */
 
 /* Device facts the host side needs for workspace sizing. */
 typedef struct qb_device_info {
@@ -241,6 +249,9 @@ int qb_softmax_bwd(const qb_softmax_bwd_args* args, qb_stream_t stream);
  * kernel stores, per row, max_j x, sum_j exp(x - max) and the raw target logit (0 when the
  * target column is outside [col_offset, col_offset + N) or ignored), and loss / lse may be NULL.
  * target holds GLOBAL class ids; col_offset is the id of this shard's first column.
+ * A target that is negative (other than ignore_index) or >= num_classes (when given) names no
+ * class: the row is treated like an ignored one instead of reading weight / target_logit out of
+ * bounds.
  * dx may alias x (in-place).
  */
 typedef struct qb_ce_fwd_args {
@@ -261,6 +272,8 @@ typedef struct qb_ce_fwd_args {
   int64_t target_logit_row_stride; /* elements; used when target_logit_ndim == 2 */
   int64_t col_offset;
   int64_t ignore_index;
+  int64_t num_classes; /* classes a target may name (length of weight, columns of a 2-D
+                          target_logit); 0 = no upper bound known */
   int32_t x_dtype;
   int32_t target_dtype; /* qb_itype */
   int32_t target_logit_dtype;
@@ -294,6 +307,7 @@ typedef struct qb_ce_bwd_args {
   int64_t dloss_stride;
   int64_t col_offset;
   int64_t ignore_index;
+  int64_t num_classes; /* as in qb_ce_fwd_args */
   int32_t x_dtype;
   int32_t dx_dtype;
   int32_t target_dtype;
@@ -320,6 +334,7 @@ typedef struct qb_ce_combine_args {
   int64_t G;
   int64_t M;
   int64_t ignore_index;
+  int64_t num_classes; /* as in qb_ce_fwd_args */
   int32_t target_dtype;
   int32_t weight_dtype;
 } qb_ce_combine_args;
@@ -378,11 +393,30 @@ typedef struct qb_norm_bwd_static_args {
 
 int qb_norm_bwd_static(const qb_norm_bwd_static_args* args, qb_stream_t stream);
 
+/*
+ * Health counter of the shared-memory ring kernels (long rows).  Every wait inside those kernels
+ * is bounded; a wait that gave up lets its kernel run to the end with wrong results for the rows
+ * concerned and increments a per-device counter.  Stores the current device's count (0 in a
+ * healthy process) into *count.  Synchronises the device (it is a diagnostic, not a hot-path
+ * call).  No counterpart in the reference, whose pipelines wait without a limit
+ * (quack/pipeline.py:400-535).
+ */
+int qb_ring_timeouts(uint32_t* count);
+
 /* Fills *info for a CUDA device ordinal (-1 = current device). */
 int qb_query_device(int32_t device, qb_device_info* info);
 
 /* Message of the last failing call made by this thread ("" if none). */
 const char* qb_last_error(void);
+
+/*
+ * Name of the device kernel (template arguments included, e.g.
+ * "void qb::norm_fwd_kernel<2, 8, 8, false, false, 1>(qb::NormFwdParams)") that the last entry
+ * point called by this host thread launched last; "" if none.  Lets a benchmark or a profile
+ * summary state which instantiation served a shape.  No counterpart in the reference, where the
+ * kernel is whatever the JIT compiled for the call.
+ */
+const char* qb_last_kernel(void);
 
 /* ABI self-description: QB_ABI_VERSION the library was built with. */
 int qb_abi_version(void);

@@ -19,7 +19,7 @@ import torch
 QB_F32, QB_F16, QB_BF16 = 0, 1, 2
 QB_I32, QB_I64 = 0, 1
 QB_OK, QB_ERR_INVALID, QB_ERR_UNSUPPORTED, QB_ERR_CUDA = 0, -1, -2, -3
-QB_ABI_VERSION = 1
+QB_ABI_VERSION = 2
 
 FLOAT_CODES = {torch.float32: QB_F32, torch.float16: QB_F16, torch.bfloat16: QB_BF16}
 INDEX_CODES = {torch.int32: QB_I32, torch.int64: QB_I64}
@@ -33,7 +33,8 @@ class LaunchCfg(Structure):
         ("max_ctas", c_int32),
         ("stages", c_int32),
         ("flags", c_int32),
-        ("reserved", c_int32 * 2),
+        ("ctas_per_sm", c_int32),
+        ("reserved", c_int32),
     ]
 
 
@@ -121,6 +122,7 @@ class CeFwdArgs(Structure):
         ("row_max", c_void_p), ("row_sumexp", c_void_p), ("row_tgt", c_void_p),
         ("M", c_int64), ("N", c_int64), ("x_row_stride", c_int64), ("dx_row_stride", c_int64),
         ("target_logit_row_stride", c_int64), ("col_offset", c_int64), ("ignore_index", c_int64),
+        ("num_classes", c_int64),
         ("x_dtype", c_int32), ("target_dtype", c_int32), ("target_logit_dtype", c_int32),
         ("target_logit_ndim", c_int32), ("weight_dtype", c_int32), ("pad0", c_int32),
         ("cfg", LaunchCfg),
@@ -133,6 +135,7 @@ class CeBwdArgs(Structure):
         ("weight", c_void_p), ("dx", c_void_p),
         ("M", c_int64), ("N", c_int64), ("x_row_stride", c_int64), ("dx_row_stride", c_int64),
         ("dloss_stride", c_int64), ("col_offset", c_int64), ("ignore_index", c_int64),
+        ("num_classes", c_int64),
         ("x_dtype", c_int32), ("dx_dtype", c_int32), ("target_dtype", c_int32),
         ("weight_dtype", c_int32), ("cfg", LaunchCfg),
     ]
@@ -142,7 +145,7 @@ class CeCombineArgs(Structure):
     _fields_ = [
         ("stats", c_void_p), ("target", c_void_p), ("weight", c_void_p),
         ("loss", c_void_p), ("lse", c_void_p),
-        ("G", c_int64), ("M", c_int64), ("ignore_index", c_int64),
+        ("G", c_int64), ("M", c_int64), ("ignore_index", c_int64), ("num_classes", c_int64),
         ("target_dtype", c_int32), ("weight_dtype", c_int32),
     ]
 
@@ -159,7 +162,7 @@ EXPORTED_SYMBOLS = (
     "qb_norm_fwd", "qb_norm_bwd", "qb_norm_bwd_num_partials", "qb_colsum", "qb_softmax_fwd",
     "qb_softmax_bwd", "qb_ce_fwd", "qb_ce_bwd", "qb_ce_combine", "qb_query_device",
     "qb_last_error", "qb_abi_version", "qb_sizeof_args", "qb_norm_bwd_static",
-    "qb_rms_final_reduce",
+    "qb_rms_final_reduce", "qb_ring_timeouts", "qb_last_kernel",
 )
 
 _LIB: Optional[ctypes.CDLL] = None
@@ -215,6 +218,10 @@ def lib() -> ctypes.CDLL:
     cdll.qb_norm_bwd_num_partials.argtypes = [c_int64, c_int32, c_int32, c_int32]
     cdll.qb_query_device.restype = ctypes.c_int
     cdll.qb_query_device.argtypes = [c_int32, POINTER(DeviceInfo)]
+    cdll.qb_last_kernel.restype = c_char_p
+    cdll.qb_last_kernel.argtypes = []
+    cdll.qb_ring_timeouts.restype = ctypes.c_int
+    cdll.qb_ring_timeouts.argtypes = [POINTER(ctypes.c_uint32)]
     _LIB = cdll
     return cdll
 
@@ -242,7 +249,7 @@ def ptr(t: Optional[torch.Tensor]) -> Optional[int]:
 
 
 def make_cfg(num_threads: int = 0, threads_per_row: int = 0, cluster_n: int = 0,
-             max_ctas: int = 0, stages: int = 0, flags: int = 0) -> LaunchCfg:
+             max_ctas: int = 0, stages: int = 0, flags: int = 0, ctas_per_sm: int = 0) -> LaunchCfg:
     cfg = LaunchCfg()
     cfg.num_threads = int(num_threads)
     cfg.threads_per_row = int(threads_per_row)
@@ -250,11 +257,13 @@ def make_cfg(num_threads: int = 0, threads_per_row: int = 0, cluster_n: int = 0,
     cfg.max_ctas = int(max_ctas)
     cfg.stages = int(stages)
     cfg.flags = int(flags)
+    cfg.ctas_per_sm = int(ctas_per_sm)
     return cfg
 
 
 def env_cfg(op: str) -> Optional[LaunchCfg]:
-    """Launch override from QUACK_B200_CFG="op:threads:threads_per_row:cluster:max_ctas:stages:flags;..."
+    """Launch override from
+    QUACK_B200_CFG="op:threads:threads_per_row:cluster:max_ctas:stages:flags:ctas_per_sm;..."
     (used by tuning sweeps; 0 keeps the heuristic for a field)."""
     spec = os.environ.get("QUACK_B200_CFG")
     if not spec:
@@ -262,8 +271,8 @@ def env_cfg(op: str) -> Optional[LaunchCfg]:
     for item in spec.split(";"):
         parts = item.split(":")
         if parts and parts[0] == op:
-            vals = [int(v) if v else 0 for v in parts[1:7]]
-            vals += [0] * (6 - len(vals))
+            vals = [int(v) if v else 0 for v in parts[1:8]]
+            vals += [0] * (7 - len(vals))
             return make_cfg(*vals)
     return None
 
@@ -314,3 +323,16 @@ def norm_bwd_num_partials(N: int, x_dtype: torch.dtype, is_layernorm: bool, devi
     if n <= 0:
         check(n if n < 0 else QB_ERR_INVALID, "qb_norm_bwd_num_partials")
     return n
+
+
+def ring_timeouts() -> int:
+    """Waits of the shared-memory ring kernels that gave up on the current device since the library
+    was loaded (0 in a healthy process).  Synchronises the device."""
+    n = ctypes.c_uint32(0)
+    check(lib().qb_ring_timeouts(byref(n)), "qb_ring_timeouts")
+    return int(n.value)
+
+
+def last_kernel() -> str:
+    """Name (with template arguments) of the device kernel this thread's last call launched last."""
+    return lib().qb_last_kernel().decode("utf-8", "replace")

@@ -25,6 +25,15 @@ def _rows(t: Tensor) -> Tensor:
     return t if t.stride(-1) == 1 or t.size(-1) == 1 else t.contiguous()
 
 
+def _num_classes(x, target_logit, weight) -> int:
+    """Upper bound of valid class ids: what the kernel may index weight / target_logit with."""
+    if weight is not None:
+        return weight.numel()
+    if target_logit is not None:
+        return target_logit.size(1) if target_logit.dim() == 2 else 0
+    return x.size(1)
+
+
 def _fill_ce_fwd(a, x, target, target_logit, loss, lse, dx, weight, ignore_index, col_offset=0):
     a.x, a.target, a.weight = _C.ptr(x), _C.ptr(target), _C.ptr(weight)
     a.loss, a.lse, a.dx = _C.ptr(loss), _C.ptr(lse), _C.ptr(dx)
@@ -33,6 +42,7 @@ def _fill_ce_fwd(a, x, target, target_logit, loss, lse, dx, weight, ignore_index
     a.dx_row_stride = dx.stride(0) if dx is not None else 0
     a.col_offset = int(col_offset)
     a.ignore_index = int(ignore_index)
+    a.num_classes = _num_classes(x, target_logit, weight)
     a.x_dtype = _C.float_code(x)
     a.target_dtype = _C.INDEX_CODES[target.dtype]
     a.weight_dtype = _C.float_code(weight)
@@ -75,6 +85,8 @@ def cross_entropy_fwd_out(
     if x.size(0) == 0:
         return
     assert loss.dtype == torch.float32 and loss.is_contiguous()
+    if loss.numel() != x.size(0):
+        raise ValueError(f"Mismatched mLoss.shape[0]: expected {x.size(0)}, got {loss.numel()}")
     x_ = _rows(x)
     target_ = target.contiguous()
     tl_ = None
@@ -87,6 +99,8 @@ def cross_entropy_fwd_out(
         lse_ = torch.empty_like(loss)
     if lse_ is not None:
         assert lse_.dtype == torch.float32 and lse_.is_contiguous()
+        if lse_.numel() != x.size(0):
+            raise ValueError(f"Mismatched mLSE.shape[0]: expected {x.size(0)}, got {lse_.numel()}")
     dx_ = dx
     if dx is not None:
         assert dx.shape == x.shape and dx.dtype == x.dtype
@@ -160,6 +174,7 @@ def _cross_entropy_backward(x, target, dloss, lse, dx, weight=None, ignore_index
     a.dloss_stride = dloss_.stride(0)  # 0 for an expanded scalar
     a.col_offset = 0
     a.ignore_index = int(ignore_index)
+    a.num_classes = w_.numel() if w_ is not None else x_.size(1)
     a.x_dtype, a.dx_dtype = _C.float_code(x_), _C.float_code(dx_)
     a.target_dtype = _C.INDEX_CODES[target_.dtype]
     a.weight_dtype = _C.float_code(w_)

@@ -1,6 +1,8 @@
 // Library-level entry points: error string, device query, ABI self-description.
+#include <cxxabi.h>
 #include <map>
 #include <mutex>
+#include <stdlib.h>
 #include <string.h>
 
 #include "host_common.h"
@@ -18,6 +20,11 @@ int set_error(int code, const char* fmt, ...) {
 }
 
 void clear_error() { g_error[0] = '\0'; }
+
+static thread_local const void* g_last_kernel = nullptr;
+static thread_local char g_last_kernel_name[512] = "";
+
+void note_launch(const void* kernel) { g_last_kernel = kernel; }
 
 static constexpr int kMaxDevices = 64;
 static DeviceFacts g_facts[kMaxDevices];
@@ -76,8 +83,7 @@ int cached_occupancy(const void* kernel, int threads, size_t smem) {
     auto it = cache.find(key);
     if (it != cache.end()) return it->second;
   }
-  if (smem > 32 * 1024)
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (smem > 32 * 1024) ensure_kernel_attributes(kernel, smem, 1);
   int occ = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, threads, smem) != cudaSuccess) {
     cudaGetLastError();
@@ -109,9 +115,7 @@ int cached_max_clusters(const void* kernel, int threads, size_t smem, int cluste
     auto it = cache.find(key);
     if (it != cache.end()) return it->second;
   }
-  if (smem > 32 * 1024)
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (cluster_n > 8) cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (smem > 32 * 1024 || cluster_n > 8) ensure_kernel_attributes(kernel, smem, cluster_n);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(cluster_n), 1, 1);
   cfg.blockDim = dim3(static_cast<unsigned>(threads), 1, 1);
@@ -131,6 +135,56 @@ int cached_max_clusters(const void* kernel, int threads, size_t smem, int cluste
   std::lock_guard<std::mutex> lock(mu);
   cache[key] = n;
   return n;
+}
+
+int ensure_kernel_attributes(const void* kernel, size_t smem, int cluster_n) {
+  struct Key {
+    const void* k; int dev;
+    bool operator<(const Key& o) const { return k != o.k ? k < o.k : dev < o.dev; }
+  };
+  struct Val { size_t smem; bool nonportable; };
+  static std::map<Key, Val> cache;
+  static std::mutex mu;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  Val& v = cache[Key{kernel, dev}];
+  if (smem > v.smem) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    v.smem = smem;
+  }
+  if (cluster_n > 8 && !v.nonportable) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    v.nonportable = true;
+  }
+  return 0;
+}
+
+// Counter of timed-out waits of the shared-memory ring kernels, one per device (the variable is
+// part of the library image on every GPU; the host needs its device address).
+__device__ unsigned int g_ring_timeouts;
+
+unsigned int* ring_timeout_counter() {
+  static unsigned int* ptrs[kMaxDevices];
+  static std::mutex mu;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    set_error(QB_ERR_CUDA, "ring: no current device");
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (ptrs[dev] == nullptr) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_ring_timeouts);
+    if (e != cudaSuccess || p == nullptr) {
+      set_error(QB_ERR_CUDA, "ring: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+      return nullptr;
+    }
+    ptrs[dev] = static_cast<unsigned int*>(p);
+  }
+  return ptrs[dev];
 }
 
 const DeviceFacts* current_device_facts() {
@@ -162,7 +216,35 @@ extern "C" int qb_query_device(int32_t device, qb_device_info* info) {
   return QB_OK;
 }
 
+extern "C" int qb_ring_timeouts(uint32_t* count) {
+  clear_error();
+  if (count == nullptr) return set_error(QB_ERR_INVALID, "ring_timeouts: null output");
+  unsigned int* p = ring_timeout_counter();
+  if (p == nullptr) return QB_ERR_CUDA;
+  unsigned int v = 0;
+  cudaError_t e = cudaMemcpy(&v, p, sizeof(v), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess)
+    return set_error(QB_ERR_CUDA, "ring_timeouts: cudaMemcpy: %s", cudaGetErrorString(e));
+  *count = v;
+  return QB_OK;
+}
+
 extern "C" const char* qb_last_error(void) { return g_error; }
+
+extern "C" const char* qb_last_kernel(void) {
+  g_last_kernel_name[0] = '\0';
+  if (g_last_kernel == nullptr) return g_last_kernel_name;
+  const char* mangled = nullptr;
+  if (cudaFuncGetName(&mangled, g_last_kernel) != cudaSuccess || mangled == nullptr) {
+    cudaGetLastError();
+    return g_last_kernel_name;
+  }
+  int status = 0;
+  char* pretty = abi::__cxa_demangle(mangled, nullptr, nullptr, &status);
+  snprintf(g_last_kernel_name, sizeof(g_last_kernel_name), "%s", status == 0 && pretty ? pretty : mangled);
+  free(pretty);
+  return g_last_kernel_name;
+}
 
 extern "C" int qb_abi_version(void) { return QB_ABI_VERSION; }
 

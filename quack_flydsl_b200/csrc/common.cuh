@@ -739,7 +739,11 @@ __device__ __forceinline__ float2 shfl_xor_f2(float2 v, int mask) {
 template <bool ROWBAR>
 __device__ __forceinline__ void row_group_sync(const RowGeom& g) {
   if constexpr (ROWBAR) {
-    if (g.tpr >= 32 && g.tpr < static_cast<int>(blockDim.x) && g.r < 15) {
+    // The choice is CTA-uniform: either every row group uses a named barrier of its own or every
+    // thread takes barrier 0.  (A CTA with more than 15 row groups, e.g. 1024 threads at 64 per
+    // row, must not mix the two: barrier 0 counts the whole CTA.)
+    if (g.tpr >= 32 && g.tpr < static_cast<int>(blockDim.x) &&
+        static_cast<int>(blockDim.x) <= 15 * g.tpr) {
       asm volatile("bar.sync %0, %1;" ::"r"(g.r + 1), "r"(g.tpr) : "memory");
       return;
     }

@@ -20,6 +20,12 @@ struct CeFwdParams {
   int flags;  // qb_launch_cfg.flags
 };
 
+// A target names a class only if it is not ignore_index and lies inside [0, num_classes) (no upper
+// bound when num_classes is 0); anything else makes the row an ignored one.
+__device__ __forceinline__ bool target_ignored(int64_t tgt, int64_t ignore_index, int64_t num_classes) {
+  return tgt == ignore_index || tgt < 0 || (num_classes > 0 && tgt >= num_classes);
+}
+
 constexpr int kCeUnroll = 4;  // chunks in flight per thread and loop iteration
 
 template <int DT, int VEC>
@@ -83,7 +89,7 @@ __global__ void __launch_bounds__(512) ce_fwd_kernel(const CeFwdParams p) {
 
     if (row_ok && g.t == 0 && g.crank == 0) {
       const int64_t tgt = load_index(a.target, row, a.target_dtype);
-      const bool ignored = tgt == a.ignore_index;
+      const bool ignored = target_ignored(tgt, a.ignore_index, a.num_classes);
       const int64_t local = tgt - a.col_offset;
       const bool owned = !ignored && local >= 0 && local < a.N;
       float tl = 0.0f;
@@ -148,7 +154,7 @@ __global__ void __launch_bounds__(T, (T >= 1024) ? 1 : (1024 / T)) ce_fwd_dx_ker
     // Row scalars (same address for all threads: broadcast loads), read before this row's dx
     // is written because dx may alias x.
     const int64_t tgt = load_index(a.target, row, a.target_dtype);
-    const bool ignored = tgt == a.ignore_index;
+    const bool ignored = target_ignored(tgt, a.ignore_index, a.num_classes);
     const int64_t local = tgt - a.col_offset;
     const bool owned = !ignored && local >= 0 && local < a.N;
     float gscale = 0.0f;  // w[target], 0 for ignored rows
@@ -298,7 +304,7 @@ __global__ void __launch_bounds__(512) ce_bwd_kernel(const CeBwdParams p) {
     if (row_ok) {
       const int64_t tgt = load_index(a.target, row, a.target_dtype);
       lse = a.lse[row];
-      if (tgt != a.ignore_index) {
+      if (!target_ignored(tgt, a.ignore_index, a.num_classes)) {
         gscale = a.dloss != nullptr ? a.dloss[row * a.dloss_stride] : 1.0f;
         if (a.weight != nullptr) gscale *= load_scalar(a.weight, tgt, a.weight_dtype);
         const int64_t local = tgt - a.col_offset;
@@ -354,7 +360,7 @@ __global__ void __launch_bounds__(256) ce_combine_kernel(const CeCombineParams p
   if (a.lse != nullptr) a.lse[row] = m + log_s;
   if (a.loss != nullptr) {
     const int64_t tgt = load_index(a.target, row, a.target_dtype);
-    const bool ignored = tgt == a.ignore_index;
+    const bool ignored = target_ignored(tgt, a.ignore_index, a.num_classes);
     float wt = 1.0f;
     if (a.weight != nullptr && !ignored) wt = load_scalar(a.weight, tgt, a.weight_dtype);
     a.loss[row] = ignored ? 0.0f : wt * ((m - t) + log_s);
@@ -595,6 +601,7 @@ extern "C" int qb_ce_fwd(const qb_ce_fwd_args* args, qb_stream_t stream) {
   b.dloss_stride = 0;
   b.col_offset = a.col_offset;
   b.ignore_index = a.ignore_index;
+  b.num_classes = a.num_classes;
   b.x_dtype = a.x_dtype;
   b.dx_dtype = a.x_dtype;
   b.target_dtype = a.target_dtype;

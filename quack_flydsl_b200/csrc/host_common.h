@@ -220,24 +220,24 @@ int resident_ctas(void (*kernel)(Params), int threads, size_t smem, int sm_count
   return per_sm * sm_count;
 }
 
+// Raises the dynamic shared-memory limit (and allows non-portable cluster sizes) of `kernel` on
+// the current device.  The attributes are set once per (kernel, device) and remembered, so the
+// per-launch cost is one map lookup.  Returns a cudaError_t as int.
+int ensure_kernel_attributes(const void* kernel, size_t smem, int cluster_n);
+
+// Remembers (per host thread) which kernel function the last launch used; qb_last_kernel() turns
+// it into a readable name on request.
+void note_launch(const void* kernel);
+
 // Launches `kernel` with an optional cluster dimension along x (grid.x must be a multiple of it).
 template <class Params>
 int launch_kernel(void (*kernel)(Params), dim3 grid, int threads, size_t smem, int cluster_n,
                   cudaStream_t stream, const Params& params, const char* name) {
-  if (smem > 32 * 1024) {  // static + dynamic shared memory above 48 KB needs the opt-in
-    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(kernel),
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) {
-      return set_error(QB_ERR_CUDA, "%s: cudaFuncSetAttribute(smem=%zu): %s", name, smem,
-                       cudaGetErrorString(e));
-    }
-  }
-  if (cluster_n > 8) {
-    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(kernel),
-                                         cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    if (e != cudaSuccess) {
-      return set_error(QB_ERR_CUDA, "%s: non-portable cluster size: %s", name,
-                       cudaGetErrorString(e));
+  if (smem > 32 * 1024 || cluster_n > 8) {  // static + dynamic shared memory above 48 KB needs the opt-in
+    const int e = ensure_kernel_attributes(reinterpret_cast<const void*>(kernel), smem, cluster_n);
+    if (e != 0) {
+      return set_error(QB_ERR_CUDA, "%s: cudaFuncSetAttribute(smem=%zu, cluster=%d): %s", name, smem,
+                       cluster_n, cudaGetErrorString(static_cast<cudaError_t>(e)));
     }
   }
   cudaLaunchConfig_t cfg = {};
@@ -254,6 +254,7 @@ int launch_kernel(void (*kernel)(Params), dim3 grid, int threads, size_t smem, i
     cfg.attrs = attr;
     cfg.numAttrs = 1;
   }
+  note_launch(reinterpret_cast<const void*>(kernel));
   cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, params);
   if (e != cudaSuccess) {
     return set_error(QB_ERR_CUDA, "%s: launch failed (grid %u x %u, block %d, cluster %d, smem %zu): %s",
@@ -277,6 +278,50 @@ int launch_persistent(void (*kernel)(Params), int64_t num_tiles, int grid_y, int
   if (clusters < 1) clusters = 1;
   dim3 grid(static_cast<unsigned>(clusters * cluster_n), static_cast<unsigned>(grid_y), 1);
   return launch_kernel(kernel, grid, threads, smem, cluster_n, stream, params, name);
+}
+
+// ---------------------------------------------------------------------------------------------
+// bulk-copy shared-memory ring (ring.cuh): host-side geometry
+// ---------------------------------------------------------------------------------------------
+// Device counter of ring waits that timed out on the current device (nullptr + error on failure).
+unsigned int* ring_timeout_counter();
+
+struct RingPlan {
+  int cluster_n = 0;     // CTAs sharing a row
+  int ns = 0;            // ring slots
+  int cols_per_cta = 0;  // columns owned by one CTA (multiple of vec)
+  int chunks_per_row = 0;  // slots one CTA's slice of a row occupies
+  size_t smem = 0;       // dynamic shared memory: control block + slots
+};
+
+// A row of N elements (esz bytes each, vec elements per 16-byte chunk) with n_in streamed inputs is
+// staged in slots of ch_bytes per input.  Picks the smallest power-of-two cluster (<= 16, or the
+// one the caller asks for) whose per-CTA slice fits the ring, and as many slots as shared memory
+// holds (at most max_slots).  Returns false if no cluster size fits.
+inline bool plan_ring(int64_t N, int vec, int esz, int n_in, int ch_bytes, int ctl_bytes,
+                      int max_smem_optin, int max_slots, int force_cluster, RingPlan* out) {
+  const int64_t slot_bytes = (int64_t)n_in * ch_bytes;
+  int64_t ns_max = ((int64_t)max_smem_optin - ctl_bytes) / slot_bytes;
+  if (ns_max > max_slots) ns_max = max_slots;
+  if (ns_max < 1) return false;
+  const int64_t chunks = N / vec;
+  for (int c = force_cluster > 0 ? force_cluster : 1; c <= 16; c <<= 1) {
+    int cl = c;
+    // every CTA of the cluster owns at least one chunk
+    while (cl > 1 && (int64_t)(cl - 1) * ceil_div(chunks, cl) >= chunks) cl >>= 1;
+    const int64_t cpc = ceil_div(chunks, cl);
+    const int64_t r = ceil_div(cpc * vec * esz, ch_bytes);
+    if (r <= ns_max) {
+      out->cluster_n = cl;
+      out->ns = static_cast<int>(ns_max);
+      out->cols_per_cta = static_cast<int>(cpc * vec);
+      out->chunks_per_row = static_cast<int>(r);
+      out->smem = static_cast<size_t>(ctl_bytes) + static_cast<size_t>(ns_max * slot_bytes);
+      return true;
+    }
+    if (force_cluster > 0) break;
+  }
+  return false;
 }
 
 }  // namespace qb

@@ -12,6 +12,7 @@
 
 #include "common.cuh"
 #include "host_common.h"
+#include "norm_bwd_ring.h"
 
 namespace qb {
 
@@ -488,6 +489,12 @@ extern "C" int qb_norm_bwd_num_partials(int64_t N, int32_t x_dtype, int32_t is_l
   vw.limit_elems(N);
   while (vw.vec * host_dtype_bytes(x_dtype) > 16) vw.vec >>= 1;
   const bool uniform = vw.vec == 16 / host_dtype_bytes(x_dtype);
+  // Shapes the bulk-copy ring kernel serves want one slice per resident cluster of that kernel
+  // (its geometry with db accumulators is the one every caller can use).
+  if (uniform && false) {
+    const int n = norm_bwd_ring_num_partials(N, x_dtype, dev);
+    if (n > 0) return n;
+  }
   NormBwdPlan plan;
   qb_launch_cfg cfg = {};
   if (int rc = plan_norm_bwd(N, vw.vec, uniform, x_dtype, false, cfg, dev, &plan)) return rc;
@@ -531,6 +538,25 @@ extern "C" int qb_norm_bwd(const qb_norm_bwd_args* args, qb_stream_t stream) {
                  (!a.dresidual || a.dresidual_dtype == a.x_dtype);
   if (vec != 16 / host_dtype_bytes(a.x_dtype)) uniform = false;
 
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // Rows staged by bulk copies into a shared-memory ring, 512 threads per row: taken when the
+  // shape fits it, the caller pinned no launch geometry and the number of partial slices does
+  // not exceed the clusters resident at once.
+  if (uniform && a.M > 0 && !(a.cfg.flags & QB_FLAG_NO_RING) && a.cfg.ctas_per_sm != 0 &&
+      a.cfg.threads_per_row == 0 && a.cfg.cluster_n == 0 && a.cfg.stages == 0) {
+    int64_t want = (a.dw_partial != nullptr || a.db_partial != nullptr)
+                       ? a.num_partials
+                       : (a.cfg.max_ctas > 0 ? a.cfg.max_ctas : 0);
+    if (want == 0) {
+      want = norm_bwd_ring_num_partials(a.N, a.x_dtype, dev);
+    }
+    if (want > 0) {
+      const int rr = launch_norm_bwd_ring(a, want, dev, st);
+      if (rr != QB_ERR_UNSUPPORTED) return rr;
+      clear_error();
+    }
+  }
+
   NormBwdPlan plan;
   if (int rc = plan_norm_bwd(a.N, vec, uniform, a.x_dtype, a.dresidual_out != nullptr, a.cfg, dev,
                              &plan))
@@ -559,7 +585,6 @@ extern "C" int qb_norm_bwd(const qb_norm_bwd_args* args, qb_stream_t stream) {
   const size_t fold_bytes =
       p.rows_per_cta > 1 ? (size_t)plan.rows.threads * plan.rows.K * vec * 4 : 0;
   if (smem < fold_bytes) smem = fold_bytes;
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
 
   if (uniform) {
     switch (a.x_dtype) {

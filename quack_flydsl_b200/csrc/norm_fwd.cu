@@ -407,6 +407,52 @@ extern "C" int qb_norm_fwd(const qb_norm_fwd_args* args, qb_stream_t stream) {
   const bool raw = uniform && a.residual == nullptr && a.residual_out == nullptr &&
                    a.x_dtype != QB_F32 && !(a.cfg.flags & 1);
 
+  NormFwdParams p;
+  p.a = a;
+  p.flags = a.cfg.flags;
+  // Long rows with at least one row per SM: the streamed two-pass kernel with the row parked in
+  // L2.  Measured on B200 (bf16, 1 GiB per tensor) it overtakes the register / cluster kernels
+  // from 64 KB per row (48 KB for LayerNorm, 128 KB with a residual, where two tensors are
+  // streamed); flag bit 4
+  // forces it for any row, flag bit 1 disables it.
+  const int64_t row_bytes = a.N * host_dtype_bytes(a.x_dtype);
+  const bool long_row =
+      row_bytes >= (a.residual != nullptr ? (128 << 10) : (a.is_layernorm ? (48 << 10) : (64 << 10)));
+  // The streamed kernel writes residual_out in its first pass and reads x / residual again in the
+  // second one, so residual_out must not overlap either input (the register kernels allow that).
+  // `out` is written in the second pass only, element by element by the thread that read the same
+  // element, so an out that IS an input (same address, same stride) is safe; a shifted overlap is
+  // not.
+  auto overlaps = [&](const void* o, int64_t o_stride, const void* in, int64_t in_stride,
+                      bool exact_alias_ok) {
+    if (o == nullptr || in == nullptr) return false;
+    if (exact_alias_ok && o == in && o_stride == in_stride) return false;
+    const int eb = host_dtype_bytes(a.x_dtype);
+    const char* o0 = static_cast<const char*>(o);
+    const char* o1 = o0 + ((a.M - 1) * o_stride + a.N) * eb;
+    const char* i0 = static_cast<const char*>(in);
+    const char* i1 = i0 + ((a.M - 1) * in_stride + a.N) * eb;
+    return o0 < i1 && i0 < o1;
+  };
+  const bool aliased =
+      overlaps(a.residual_out, a.residual_out_row_stride, a.x, a.x_row_stride, false) ||
+      overlaps(a.residual_out, a.residual_out_row_stride, a.residual, a.residual_row_stride, false) ||
+      overlaps(a.out, a.out_row_stride, a.x, a.x_row_stride, true) ||
+      overlaps(a.out, a.out_row_stride, a.residual, a.residual_row_stride, true);
+  if (uniform && a.H == 1 && a.cfg.cluster_n == 0 && !(a.cfg.flags & 2) && a.M >= dev->sm_count &&
+      !aliased && (long_row || (a.cfg.flags & 16))) {
+    // CTA sizes that exist: 256 and 512 threads (a caller's hint is rounded to one of them).
+    const int t = a.cfg.num_threads > 0 ? (a.cfg.num_threads > 256 ? 512 : 256)
+                                        : (a.residual != nullptr ? 512 : 256);
+    p.tpr = t;
+    p.rows_per_cta = 1;
+    p.cluster_n = 1;
+    p.cols_per_cta = static_cast<int>(a.N);
+    p.num_tiles = a.M;
+    p.stage_params = 0;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    return launch_norm_fwd_stream_any(p, t, dev, st);
+  }
   // Per-thread capacity in row elements: fp32-held rows 64 (<= 512 threads) / 16 (1024 threads);
   // packed 16-bit rows twice that; the generic mixed-dtype path (wider staging registers) 32.
   RowPlan plan;
@@ -423,41 +469,6 @@ extern "C" int qb_norm_fwd(const qb_norm_fwd_args* args, qb_stream_t stream) {
   const int K = plan.K;
   const int threads = plan.threads;
 
-  NormFwdParams p;
-  p.a = a;
-  p.flags = a.cfg.flags;
-  // Long rows with at least one row per SM: the streamed two-pass kernel with the row parked in
-  // L2.  Measured on B200 (bf16, 1 GiB per tensor) it overtakes the register / cluster kernels
-  // from 64 KB per row (48 KB for LayerNorm, 128 KB with a residual, where two tensors are
-  // streamed); flag bit 4
-  // forces it for any row, flag bit 1 disables it.
-  const int64_t row_bytes = a.N * host_dtype_bytes(a.x_dtype);
-  const bool long_row =
-      row_bytes >= (a.residual != nullptr ? (128 << 10) : (a.is_layernorm ? (48 << 10) : (64 << 10)));
-  // The streamed kernel writes residual_out in its first pass and reads x / residual again in the
-  // second one, so residual_out must not overlap either input (the register kernels allow that).
-  auto overlaps = [&](const void* in, int64_t in_stride) {
-    if (a.residual_out == nullptr || in == nullptr) return false;
-    const int eb = host_dtype_bytes(a.x_dtype);
-    const char* o0 = static_cast<const char*>(a.residual_out);
-    const char* o1 = o0 + ((a.M - 1) * a.residual_out_row_stride + a.N) * eb;
-    const char* i0 = static_cast<const char*>(in);
-    const char* i1 = i0 + ((a.M - 1) * in_stride + a.N) * eb;
-    return o0 < i1 && i0 < o1;
-  };
-  const bool aliased = overlaps(a.x, a.x_row_stride) || overlaps(a.residual, a.residual_row_stride);
-  if (uniform && a.H == 1 && a.cfg.cluster_n == 0 && !(a.cfg.flags & 2) && a.M >= dev->sm_count &&
-      !aliased && (long_row || (a.cfg.flags & 16))) {
-    const int t = a.cfg.num_threads > 0 ? a.cfg.num_threads : (a.residual != nullptr ? 512 : 256);
-    p.tpr = t;
-    p.rows_per_cta = 1;
-    p.cluster_n = 1;
-    p.cols_per_cta = static_cast<int>(a.N);
-    p.num_tiles = a.M;
-    p.stage_params = 0;
-    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    return launch_norm_fwd_stream_any(p, t, dev, st);
-  }
   p.tpr = plan.tpr;
   p.rows_per_cta = plan.rows_per_cta;
   p.cluster_n = plan.cluster_n;

@@ -9,21 +9,9 @@
 
 #include "common.cuh"
 #include "host_common.h"
+#include "softmax.h"
 
 namespace qb {
-
-struct SoftmaxParams {
-  const void* in0;  // fwd: x        bwd: dy
-  const void* in1;  // fwd: unused   bwd: y
-  void* out;        // fwd: y        bwd: dx
-  int64_t M;
-  int N;
-  int64_t ld0, ld1, ldo;
-  int dt0, dt1, dto;
-  int tpr, rows_per_cta, cluster_n, cols_per_cta;
-  int64_t num_tiles;
-  int flags;  // qb_launch_cfg.flags
-};
 
 // RAW (16-bit inputs): the row stays packed in registers (twice the bytes in flight per register)
 // and is unpacked by each pass; the exponential is then evaluated twice per element (once for the
@@ -472,6 +460,17 @@ static int softmax_dispatch(SoftmaxParams& p, bool uniform, int vec, const qb_la
     const int rc = plan_rows(opname, p.N, vec, caps, pref, k_target, 128, qb_launch_cfg{}, &probe);
     if (rc != QB_OK || probe.cluster_n > 1) {
       clear_error();
+      // Long rows.  Backward: staged once in a shared-memory ring by bulk copies (measured on
+      // B200, bf16: +2 % at N = 65536, +4 % at 131072, +12 % at 40960, +17 % at 262144 over
+      // re-reading the row from L2).  Forward: the L2 kernel; the ring version is within 1 % of
+      // it from N = 65536 and slower below (both are bound by the special function unit: two ex2
+      // per element), so it only runs when asked for.  What the ring cannot hold falls through.
+      const bool want_ring = BWD ? !(cfg.flags & QB_FLAG_NO_RING) : (cfg.flags & QB_FLAG_RING_FWD) != 0;
+      if (want_ring) {
+        const int rr = launch_softmax_ring<BWD>(p, cfg, dev, st);
+        if (rr != QB_ERR_UNSUPPORTED) return rr;
+        clear_error();
+      }
       return launch_softmax_stream<BWD>(p, cfg, dev, st);
     }
   }

@@ -117,6 +117,13 @@ def _launch_norm_fwd(x, weight, out, bias, rstd, mean, residual, residual_out, e
     for name, t in (("mO", out), ("mRes", residual), ("mResO", residual_out)):
         if t is not None and t.shape != x.shape:
             raise ValueError(f"Mismatched {name}.shape: expected {tuple(x.shape)}, got {tuple(t.shape)}")
+    rows = x.numel() // N if N else 0
+    for name, t in (("mRstd", rstd), ("mMean", mean)):
+        # per-row statistics are written as fp32: a narrower or shorter buffer would be overrun
+        if t is not None and t.dtype != torch.float32:
+            raise ValueError(f"Mismatched {name}.dtype: expected torch.float32, got {t.dtype}")
+        if t is not None and t.numel() != rows:
+            raise ValueError(f"Mismatched {name}.shape[0] on argument {name}: expected {rows}, got {t.numel()}")
     if x.numel() == 0:
         return
     _compile_rmsnorm_fwd.note((
@@ -239,10 +246,16 @@ def _launch_norm_bwd(x, weight, dout, rstd, dx, dw_partial, db_partial, dresidua
     for name, t in (("mX", x), ("mW", weight), ("mdO", dout), ("mRstd", rstd), ("mdX", dx)):
         if t is not None:
             _C.require_cuda(t, name)
+    N = x.size(-1)
+    rows = x.numel() // N if N else 0
+    for name, t in (("mRstd", rstd), ("mMean", mean)):
+        if t is not None and t.dtype != torch.float32:
+            raise ValueError(f"Mismatched {name}.dtype: expected torch.float32, got {t.dtype}")
+        if t is not None and t.numel() != rows:
+            raise ValueError(f"Mismatched {name}.shape[0] on argument {name}: expected {rows}, got {t.numel()}")
     if x.numel() == 0:
         return
     per_head = x.dim() == 3
-    N = x.size(-1)
     H = x.size(1) if per_head else 1
     if weight is not None and weight.size(-1) != N:
         raise ValueError(f"Mismatched mW.shape[0] on argument mW: expected {N}, got {weight.size(-1)}")
@@ -578,3 +591,62 @@ class QuackRMSNorm(torch.nn.RMSNorm):
 
     def forward(self, x: Tensor) -> Tensor:
         return rmsnorm(x, self.weight, eps=self.eps)
+
+
+# ---------------------------------------------------------------------------------------------
+# plain PyTorch reference functions (public in the reference module: quack/rmsnorm.py:563-594,
+# :1727-1741; its own tests import them from here)
+# ---------------------------------------------------------------------------------------------
+def rmsnorm_ref(x, w=None, bias=None, residual=None, eps=1e-6, weight_offset=0.0):
+    """fp32 RMSNorm in plain PyTorch: normalises ``x + residual`` by its root mean square, scales
+    by ``w + weight_offset``, adds ``bias``; the result is cast to ``x.dtype``.  With a residual
+    returns ``(out, (x + residual).to(residual.dtype))``."""
+    h = x.float()
+    if residual is not None:
+        h = h + residual.float()
+    y = h / torch.sqrt(h.square().mean(dim=-1, keepdim=True) + eps)
+    if w is not None:
+        y = y * (w.float() + weight_offset)
+    if bias is not None:
+        y = y + bias.float()
+    if residual is None:
+        return y.to(x.dtype)
+    return y.to(x.dtype), h.to(residual.dtype)
+
+
+def rmsnorm_bwd_ref(x, w, dout, rstd, eps=1e-6, weight_offset=0.0):
+    """Plain PyTorch RMSNorm backward from a saved ``rstd`` (M,): returns ``(dx, dw)`` with ``dw``
+    None when there is no weight.  ``eps`` is unused (rstd already contains it)."""
+    xhat = x.float() * rstd.unsqueeze(1)
+    wdy = dout * (w.float() + weight_offset) if w is not None else dout
+    dx = (wdy - xhat * (xhat * wdy).mean(dim=-1, keepdim=True)) * rstd.unsqueeze(1)
+    if w is None:
+        return dx.to(x.dtype), None
+    return dx.to(x.dtype), (dout * xhat).sum(dim=0).to(w.dtype)
+
+
+def layernorm_ref(x: Tensor, w: Tensor, eps: float = 1e-6) -> Tensor:
+    """``F.layer_norm`` on the fp32 upcast of x with weight ``w`` and no bias, cast to x.dtype."""
+    return torch.nn.functional.layer_norm(x.float(), w.shape, w, None, eps).to(x.dtype)
+
+
+def layernorm_rstd_ref(x: Tensor, eps: float = 1e-6) -> Tensor:
+    """1 / sqrt(biased variance + eps) of every row, fp32."""
+    xf = x.float()
+    centred = xf - xf.mean(dim=-1, keepdim=True)
+    return 1.0 / torch.sqrt(centred.square().mean(dim=-1) + eps)
+
+
+def layernorm_mean_ref(x: Tensor) -> Tensor:
+    """Row means in fp32."""
+    return x.float().mean(dim=-1)
+
+
+def __getattr__(name):
+    # layernorm_fwd / layernorm_bwd are defined in quack/rmsnorm.py in the reference
+    # (:1625-1724); here they live in the layernorm module, which imports this one.
+    if name in ("layernorm_fwd", "layernorm_bwd", "layernorm"):
+        import importlib
+
+        return getattr(importlib.import_module("quack_flydsl_b200.layernorm"), name)
+    raise AttributeError(f"module {__name__!r} has no attribute {name!r}")

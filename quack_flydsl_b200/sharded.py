@@ -153,6 +153,7 @@ def ce_combine(stats_all: Tensor, target: Tensor, weight: Optional[Tensor] = Non
     a.loss, a.lse = _C.ptr(loss), _C.ptr(lse)
     a.G, a.M = G, M
     a.ignore_index = int(ignore_index)
+    a.num_classes = w_.numel() if w_ is not None else 0
     a.target_dtype = _C.INDEX_CODES[t_.dtype]
     a.weight_dtype = _C.float_code(w_)
     with _C.device_of(s_):
@@ -179,6 +180,7 @@ def ce_shard_bwd(x_shard, target, dloss, lse, col_offset, weight=None, ignore_in
     a.dloss_stride = dl.stride(0)
     a.col_offset = int(col_offset)
     a.ignore_index = int(ignore_index)
+    a.num_classes = w_.numel() if w_ is not None else 0
     a.x_dtype, a.dx_dtype = _C.float_code(x_), _C.float_code(dx)
     a.target_dtype = _C.INDEX_CODES[t_.dtype]
     a.weight_dtype = _C.float_code(w_)
