@@ -291,9 +291,15 @@ class Timeline:
 
 def time_kernel(fn, iters=20, warmup=3):
     """Median device time of fn() in ms over ``iters`` launches, one CUDA-event pair per launch
-    (inputs exceed L2)."""
-    for _ in range(warmup):
+    (inputs exceed L2).  Warm-up: at least ``warmup`` launches and at least 100 ms of them, so that
+    a kernel measured right after its inputs were generated does not carry that phase's clocks."""
+    t0 = time.perf_counter()
+    n = 0
+    while n < warmup or time.perf_counter() - t0 < 0.1:
         fn()
+        n += 1
+        if n % 8 == 0:
+            torch.cuda.synchronize()
     torch.cuda.synchronize()
     # Queue the launches behind ~15 ms of GPU-side sleep: several of these kernels are shorter than
     # the host-side launch path, and an event pair around a launch on an idle stream would time

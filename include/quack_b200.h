@@ -362,6 +362,53 @@ typedef struct qb_rms_final_reduce_args {
 int qb_rms_final_reduce(const qb_rms_final_reduce_args* args, qb_stream_t stream);
 
 /*
+ * Top-k over the last dimension of an (M, N) matrix, largest first, optionally followed by a
+ * softmax over the k selected values.
+ * Replaces the compiled TopK kernel called by quack::_topk_fwd (quack/topk.py:234-254, kernel
+ * quack/topk.py:26-233).  N must be a power of two <= 4096 and k <= 128 (the reference's
+ * contract); values (M, k) has x's dtype, indices (M, k) is int32; both contiguous.  Equal values
+ * come out in order of increasing column.
+ */
+typedef struct qb_topk_fwd_args {
+  const void* x;
+  void* values;
+  int32_t* indices;
+  int64_t M;
+  int64_t N;
+  int64_t k;
+  int64_t x_row_stride;
+  int32_t x_dtype;
+  int32_t softmax; /* 0 / 1 */
+} qb_topk_fwd_args;
+
+int qb_topk_fwd(const qb_topk_fwd_args* args, qb_stream_t stream);
+
+/*
+ * Top-k backward: every row of dx (M, N) is written completely -- zeros, then
+ *   dx[r, indices[r, j]] = dvalues[r, j]                                        (softmax == 0)
+ *   dx[r, indices[r, j]] = values[r, j] * (dvalues[r, j] - sum_i dvalues[r, i] * values[r, i])
+ * where values is the forward's (softmaxed) output.  Replaces the compiled TopKBackward kernel
+ * called by quack::_topk_bwd (quack/topk.py:461-491, kernel quack/topk.py:275-460).  dvalues,
+ * values and indices are (M, k) contiguous; dx has unit column stride.
+ */
+typedef struct qb_topk_bwd_args {
+  const void* dvalues;
+  const void* values; /* required iff softmax */
+  const int32_t* indices;
+  void* dx;
+  int64_t M;
+  int64_t N;
+  int64_t k;
+  int64_t dx_row_stride;
+  int32_t dvalues_dtype;
+  int32_t values_dtype;
+  int32_t dx_dtype;
+  int32_t softmax;
+} qb_topk_bwd_args;
+
+int qb_topk_bwd(const qb_topk_bwd_args* args, qb_stream_t stream);
+
+/*
  * Norm backward without a caller-provided workspace.  No counterpart in the reference (there the
  * caller always allocates dw_partial / db_partial with torch, quack/rmsnorm.py:1368-1379); added
  * for hosts that may not allocate device memory: code running after an application's "memory is
@@ -425,7 +472,7 @@ int qb_abi_version(void);
  * sizeof() of an argument block as compiled into the library, so a foreign-language binding can
  * verify its struct layout before the first call.  which: 0 launch_cfg, 1 norm_fwd, 2 norm_bwd,
  * 3 colsum, 4 softmax_fwd, 5 softmax_bwd, 6 ce_fwd, 7 ce_bwd, 8 ce_combine, 9 device_info,
- * 10 norm_bwd_static, 11 rms_final_reduce.
+ * 10 norm_bwd_static, 11 rms_final_reduce, 12 topk_fwd, 13 topk_bwd.
  * Returns -1 for an unknown code.
  */
 int qb_sizeof_args(int32_t which);

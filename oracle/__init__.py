@@ -31,4 +31,5 @@ from oracle.cross_entropy import (  # noqa: F401
     cross_entropy_shard_stats_ref,
 )
 from oracle.linear_cross_entropy import linear_cross_entropy_ref, rms_final_reduce_ref  # noqa: F401
+from oracle.topk import topk_bwd_ref, topk_ref  # noqa: F401
 from oracle.util import bf16_ulp_diff, make_config_inputs  # noqa: F401

@@ -10,6 +10,6 @@ from quack_flydsl_b200 import *  # noqa: F401,F403
 from quack_flydsl_b200 import __all__, __version__  # noqa: F401
 
 for _name in ("rmsnorm", "rmsnorm_config", "layernorm", "softmax", "cross_entropy", "rounding",
-              "sharded", "linear_cross_entropy", "rms_final_reduce", "cute_dsl_utils", "dsl",
+              "sharded", "linear_cross_entropy", "rms_final_reduce", "cute_dsl_utils", "topk", "dsl",
               "dsl.torch_library_op"):
     _sys.modules[f"quack.{_name}"] = _importlib.import_module(f"quack_flydsl_b200.{_name}")

@@ -150,11 +150,24 @@ class CeCombineArgs(Structure):
     ]
 
 
+class TopkFwdArgs(Structure):
+    _fields_ = [("x", c_void_p), ("values", c_void_p), ("indices", c_void_p),
+                ("M", c_int64), ("N", c_int64), ("k", c_int64), ("x_row_stride", c_int64),
+                ("x_dtype", c_int32), ("softmax", c_int32)]
+
+
+class TopkBwdArgs(Structure):
+    _fields_ = [("dvalues", c_void_p), ("values", c_void_p), ("indices", c_void_p), ("dx", c_void_p),
+                ("M", c_int64), ("N", c_int64), ("k", c_int64), ("dx_row_stride", c_int64),
+                ("dvalues_dtype", c_int32), ("values_dtype", c_int32), ("dx_dtype", c_int32),
+                ("softmax", c_int32)]
+
+
 # code passed to qb_sizeof_args -> the Structure that must have that size
 _SIZEOF_CODES = {
     0: LaunchCfg, 1: NormFwdArgs, 2: NormBwdArgs, 3: ColsumArgs, 4: SoftmaxFwdArgs,
     5: SoftmaxBwdArgs, 6: CeFwdArgs, 7: CeBwdArgs, 8: CeCombineArgs, 9: DeviceInfo,
-    10: NormBwdStaticArgs, 11: RmsFinalReduceArgs,
+    10: NormBwdStaticArgs, 11: RmsFinalReduceArgs, 12: TopkFwdArgs, 13: TopkBwdArgs,
 }
 
 # every symbol include/quack_b200.h declares
@@ -162,7 +175,7 @@ EXPORTED_SYMBOLS = (
     "qb_norm_fwd", "qb_norm_bwd", "qb_norm_bwd_num_partials", "qb_colsum", "qb_softmax_fwd",
     "qb_softmax_bwd", "qb_ce_fwd", "qb_ce_bwd", "qb_ce_combine", "qb_query_device",
     "qb_last_error", "qb_abi_version", "qb_sizeof_args", "qb_norm_bwd_static",
-    "qb_rms_final_reduce", "qb_ring_timeouts", "qb_last_kernel",
+    "qb_rms_final_reduce", "qb_ring_timeouts", "qb_last_kernel", "qb_topk_fwd", "qb_topk_bwd",
 )
 
 _LIB: Optional[ctypes.CDLL] = None
@@ -210,6 +223,7 @@ def lib() -> ctypes.CDLL:
         ("qb_softmax_fwd", SoftmaxFwdArgs), ("qb_softmax_bwd", SoftmaxBwdArgs),
         ("qb_ce_fwd", CeFwdArgs), ("qb_ce_bwd", CeBwdArgs), ("qb_ce_combine", CeCombineArgs),
         ("qb_norm_bwd_static", NormBwdStaticArgs), ("qb_rms_final_reduce", RmsFinalReduceArgs),
+        ("qb_topk_fwd", TopkFwdArgs), ("qb_topk_bwd", TopkBwdArgs),
     ):
         fn = getattr(cdll, name)
         fn.restype = ctypes.c_int
@@ -265,16 +279,20 @@ def env_cfg(op: str) -> Optional[LaunchCfg]:
     """Launch override from
     QUACK_B200_CFG="op:threads:threads_per_row:cluster:max_ctas:stages:flags:ctas_per_sm;..."
     (used by tuning sweeps; 0 keeps the heuristic for a field)."""
+    global _ENV_CFG_CACHE
     spec = os.environ.get("QUACK_B200_CFG")
     if not spec:
         return None
-    for item in spec.split(";"):
-        parts = item.split(":")
-        if parts and parts[0] == op:
-            vals = [int(v) if v else 0 for v in parts[1:8]]
-            vals += [0] * (7 - len(vals))
-            return make_cfg(*vals)
-    return None
+    if _ENV_CFG_CACHE[0] != spec:
+        parsed = {}
+        for item in spec.split(";"):
+            parts = item.split(":")
+            if parts and parts[0]:
+                vals = [int(v) if v else 0 for v in parts[1:8]]
+                vals += [0] * (7 - len(vals))
+                parsed[parts[0]] = make_cfg(*vals)
+        _ENV_CFG_CACHE = (spec, parsed)
+    return _ENV_CFG_CACHE[1].get(op)
 
 
 def require_cuda(t: torch.Tensor, name: str) -> None:
@@ -286,7 +304,28 @@ def require_cuda(t: torch.Tensor, name: str) -> None:
 
 
 def stream_of(t: torch.Tensor) -> int:
-    return torch.cuda.current_stream(t.device).cuda_stream
+    return torch._C._cuda_getCurrentRawStream(t.get_device())
+
+
+def launch(fn, args, t: torch.Tensor, what: str) -> None:
+    """Calls ``fn(byref(args), stream)`` with ``t``'s device current and on torch's current stream
+    of that device; raises on a negative status.  The lean form of
+    ``with device_of(t): check(fn(byref(args), stream_of(t)), what)`` for the per-call hot path."""
+    idx = t.get_device()
+    cur = torch._C._cuda_getDevice()
+    if cur == idx:
+        rc = fn(byref(args), torch._C._cuda_getCurrentRawStream(idx))
+    else:
+        torch.cuda.set_device(idx)
+        try:
+            rc = fn(byref(args), torch._C._cuda_getCurrentRawStream(idx))
+        finally:
+            torch.cuda.set_device(cur)
+    if rc != QB_OK:
+        check(rc, what)
+
+
+_ENV_CFG_CACHE = (None, {})
 
 
 class device_of:

@@ -51,7 +51,9 @@ def _fill_ce_fwd(a, x, target, target_logit, loss, lse, dx, weight, ignore_index
         a.target_logit_dtype = _C.float_code(target_logit)
         a.target_logit_ndim = target_logit.dim()
         a.target_logit_row_stride = target_logit.stride(0) if target_logit.dim() == 2 else 0
-    a.cfg = _C.env_cfg("ce_fwd") or _C.make_cfg()
+    cfg = _C.env_cfg("ce_fwd")
+    if cfg is not None:
+        a.cfg = cfg
 
 
 @kernel_op("quack::cross_entropy_fwd_out", mutates_args={"loss", "lse", "dx"})
@@ -108,8 +110,7 @@ def cross_entropy_fwd_out(
             dx_ = torch.empty_like(dx, memory_format=torch.contiguous_format)
     a = _C.CeFwdArgs()
     _fill_ce_fwd(a, x_, target_, tl_, loss, lse_, dx_, w_, ignore_index)
-    with _C.device_of(x_):
-        _C.check(_C.lib().qb_ce_fwd(byref(a), _C.stream_of(x_)), "cross_entropy_fwd")
+    _C.launch(_C.lib().qb_ce_fwd, a, x_, "cross_entropy_fwd")
     if dx is not None and dx_ is not dx:
         dx.copy_(dx_)
 
@@ -178,9 +179,10 @@ def _cross_entropy_backward(x, target, dloss, lse, dx, weight=None, ignore_index
     a.x_dtype, a.dx_dtype = _C.float_code(x_), _C.float_code(dx_)
     a.target_dtype = _C.INDEX_CODES[target_.dtype]
     a.weight_dtype = _C.float_code(w_)
-    a.cfg = _C.env_cfg("ce_bwd") or _C.make_cfg()
-    with _C.device_of(x_):
-        _C.check(_C.lib().qb_ce_bwd(byref(a), _C.stream_of(x_)), "cross_entropy_bwd")
+    cfg = _C.env_cfg("ce_bwd")
+    if cfg is not None:
+        a.cfg = cfg
+    _C.launch(_C.lib().qb_ce_bwd, a, x_, "cross_entropy_bwd")
     if dx_ is not dx:
         dx.copy_(dx_)
 

@@ -262,6 +262,8 @@ extern "C" int qb_sizeof_args(int32_t which) {
     case 9: return (int)sizeof(qb_device_info);
     case 10: return (int)sizeof(qb_norm_bwd_static_args);
     case 11: return (int)sizeof(qb_rms_final_reduce_args);
+    case 12: return (int)sizeof(qb_topk_fwd_args);
+    case 13: return (int)sizeof(qb_topk_bwd_args);
     default: return -1;
   }
 }

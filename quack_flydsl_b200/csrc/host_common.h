@@ -266,12 +266,15 @@ int launch_kernel(void (*kernel)(Params), dim3 grid, int threads, size_t smem, i
 // Launch of a kernel that walks over `num_tiles` row tiles with a grid-stride loop: the grid is
 // min(num_tiles, CTAs resident on the device) clusters (max_ctas > 0 overrides the cap), times
 // grid_y independent slices (heads).
+// per_sm_cap > 0 limits the CTAs per SM below what fits (cluster_n == 1 only).
 template <class Params>
 int launch_persistent(void (*kernel)(Params), int64_t num_tiles, int grid_y, int threads,
                       size_t smem, int cluster_n, int max_ctas, int sm_count, cudaStream_t stream,
-                      const Params& params, const char* name) {
+                      const Params& params, const char* name, int per_sm_cap = 0) {
   int64_t cap = max_ctas > 0 ? max_ctas / cluster_n
                              : resident_clusters(kernel, threads, smem, cluster_n, sm_count);
+  if (max_ctas <= 0 && per_sm_cap > 0 && cluster_n == 1 && cap > (int64_t)per_sm_cap * sm_count)
+    cap = (int64_t)per_sm_cap * sm_count;
   if (grid_y > 1 && max_ctas <= 0) cap = (cap + grid_y - 1) / grid_y;
   if (cap < 1) cap = 1;
   int64_t clusters = num_tiles < cap ? num_tiles : cap;

@@ -489,9 +489,8 @@ extern "C" int qb_norm_bwd_num_partials(int64_t N, int32_t x_dtype, int32_t is_l
   vw.limit_elems(N);
   while (vw.vec * host_dtype_bytes(x_dtype) > 16) vw.vec >>= 1;
   const bool uniform = vw.vec == 16 / host_dtype_bytes(x_dtype);
-  // Shapes the bulk-copy ring kernel serves want one slice per resident cluster of that kernel
-  // (its geometry with db accumulators is the one every caller can use).
-  if (uniform && false) {
+  // Shapes the bulk-copy ring kernel serves want one slice per resident cluster of that kernel.
+  if (uniform) {
     const int n = norm_bwd_ring_num_partials(N, x_dtype, dev);
     if (n > 0) return n;
   }
@@ -539,10 +538,11 @@ extern "C" int qb_norm_bwd(const qb_norm_bwd_args* args, qb_stream_t stream) {
   if (vec != 16 / host_dtype_bytes(a.x_dtype)) uniform = false;
 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  // Rows staged by bulk copies into a shared-memory ring, 512 threads per row: taken when the
-  // shape fits it, the caller pinned no launch geometry and the number of partial slices does
-  // not exceed the clusters resident at once.
-  if (uniform && a.M > 0 && !(a.cfg.flags & QB_FLAG_NO_RING) && a.cfg.ctas_per_sm != 0 &&
+  // Rows of three 16-byte chunks per thread (N = 6144, 12288, 24576, ... for 16-bit dtypes):
+  // staged by bulk copies into a shared-memory ring with the whole CTA on one row (see
+  // norm_bwd_ring.cu for the measurements).  Taken when the caller pinned no launch geometry and
+  // the number of partial slices does not exceed the clusters resident at once.
+  if (uniform && a.M > 0 && !(a.cfg.flags & QB_FLAG_NO_RING) && a.cfg.num_threads == 0 &&
       a.cfg.threads_per_row == 0 && a.cfg.cluster_n == 0 && a.cfg.stages == 0) {
     int64_t want = (a.dw_partial != nullptr || a.db_partial != nullptr)
                        ? a.num_partials

@@ -1,18 +1,23 @@
 // RMSNorm / LayerNorm backward, stage 1, with the rows staged by bulk asynchronous copies.
 //
 // Same mathematics and the same [P, N] partial-sum contract as norm_bwd_kernel (norm_bwd.cu,
-// after quack/rmsnorm.py:723-1205); what differs is how the data reach the arithmetic.  A producer
-// warp streams x and dout into a shared-memory ring with cp.async.bulk (the TMA path the
-// reference's Blackwell heuristic turns on for this kernel, quack/rmsnorm_config.py:226-240,
-// quack/rmsnorm.py:686-693,931-950); 512 consumer threads share each row, so a thread owns few
-// columns and the fp32 weight / dw / db registers shrink from 192 to 24 ... 96 per thread.  The
-// price of wide rows -- a reduction over 16 warps per row -- is paid once per ring slot: a slot
-// holds RPS rows, whose partial sums are reduced together (value-halving shuffles, one mbarrier
-// exchange across the warps and, for long rows, across the CTAs of a cluster).
+// after quack/rmsnorm.py:723-1205); what differs is how the data reach the arithmetic.  Thread 0
+// streams x and dout into a shared-memory ring with cp.async.bulk (the TMA path the reference's
+// Blackwell heuristic turns on for this kernel, quack/rmsnorm_config.py:226-240,
+// quack/rmsnorm.py:686-693,931-950); all 256 or 512 threads of the CTA share each row, so a
+// thread owns few columns and the fp32 weight / dw / db registers shrink from 192 to 72 per
+// thread.  The price of wide rows -- a reduction over 8 or 16 warps per row -- is one mbarrier
+// exchange across the warps and, for long rows, across the CTAs of a cluster.
 //
-// Served: one dtype for x / dout / dx with full 16-byte chunks, no residual-gradient streams,
-// H == 1, N = cluster_n * KC * 512 * (16 / element size) with KC in 1 .. 4.  Everything else
-// stays on norm_bwd_kernel.
+// Measured against norm_bwd_kernel on B200 (bf16, 512 MiB per tensor, LayerNorm / RMSNorm GB/s):
+// N = 4096: 5417 / 5612 against 5687 / 6166; N = 8192: 5135 / 5492 against 5773 / 6235;
+// N = 16384: 4972 / 5201 against 5416 / 5994 -- the cp.async kernel keeps those.  Rows of three
+// 16-byte chunks per thread, which leave a quarter of the cp.async kernel's power-of-two tile
+// empty, go the other way: N = 6144: 4939 / 4732 against 4293 / 4819; N = 12288: 4413 / 5203
+// against 4091 / 4648; N = 24576: 4223 / 4940 against 3349 / 3687.  This kernel therefore serves
+// exactly those: one dtype for x / dout / dx with full 16-byte chunks, no residual-gradient
+// streams, H == 1, N = cluster_n * 3 * T * (16 / element size) with T = 512 (cluster_n 1, 2, 4)
+// or T = 256 (cluster_n 1).
 #include <type_traits>
 
 #include "ring.cuh"
@@ -286,7 +291,7 @@ __global__ void __launch_bounds__(T, 512 / T) norm_bwd_ring_kernel(const NormBwd
 // host side
 // ---------------------------------------------------------------------------------------------
 template <int KC>
-struct RowsPerSlot {
+struct RowsPerSlot {  // rows per ring slot: about 48 KB of x + dout per slot
   static constexpr int value = KC == 1 ? 4 : (KC == 2 ? 2 : 1);
 };
 
@@ -296,37 +301,28 @@ struct NbrPlan {
   size_t smem;
 };
 
-// Geometry of the ring kernel for a row of N elements, or false if it does not apply.  The same
-// geometry serves every variant (with or without db, RMSNorm or LayerNorm), so that the number
-// of partial-sum slices a caller sizes its workspace with does not depend on them.
+// Geometry of the ring kernel for a row of N elements with `threads` per CTA, or false if it
+// does not apply.  The same geometry serves every variant (with or without db, RMSNorm or
+// LayerNorm), so the number of partial-sum slices does not depend on them.
 static bool plan_norm_bwd_ring(int64_t N, int x_dtype, int threads, int max_smem_optin, NbrPlan* out) {
   const int vec = 16 / host_dtype_bytes(x_dtype);
   const int per_sm = 512 / threads;
-  const int64_t unit = static_cast<int64_t>(threads) * vec;  // columns of one chunk round
+  const int64_t unit = static_cast<int64_t>(threads) * vec * 3;  // columns of one CTA: KC = 3
   if (N % unit != 0) return false;
-  const int64_t rounds = N / unit;  // cluster_n * KC
+  const int64_t c = N / unit;
+  if (!is_pow2(c) || c > (threads == 512 ? 4 : 1)) return false;
   const int smem_cap = per_sm == 1 ? max_smem_optin : (max_smem_optin + 1024) / per_sm - 1024;
-  // chunks per thread the registers allow: fp32 weight + dw + db accumulators, 128 registers
-  const int kc_max = 3;
-  for (int c = 1; c <= 16; c <<= 1) {
-    if (rounds % c != 0) continue;
-    const int64_t kc = rounds / c;
-    if (kc > kc_max) continue;
-    if (kc < 1) break;
-    const int rps = kc == 1 ? 4 : (kc == 2 ? 2 : 1);
-    const size_t slot = static_cast<size_t>(2) * rps * kc * threads * 16;
-    const size_t red = static_cast<size_t>(2) * (threads / 32) * c * 8 * sizeof(float);
-    int ns = static_cast<int>((static_cast<size_t>(smem_cap) - kRingCtlBytes - red) / slot);
-    if (ns > 4) ns = 4;
-    if (ns < 2) continue;
-    out->threads = threads;
-    out->cluster_n = c;
-    out->kc = static_cast<int>(kc);
-    out->ns = ns;
-    out->smem = kRingCtlBytes + static_cast<size_t>(ns) * slot + red;
-    return true;
-  }
-  return false;
+  const size_t slot = static_cast<size_t>(2) * 3 * threads * 16;  // one row: x and dout
+  const size_t red = static_cast<size_t>(2) * (threads / 32) * c * 8 * sizeof(float);
+  int ns = static_cast<int>((static_cast<size_t>(smem_cap) - kRingCtlBytes - red) / slot);
+  if (ns > 4) ns = 4;
+  if (ns < 2) return false;
+  out->threads = threads;
+  out->cluster_n = static_cast<int>(c);
+  out->kc = 3;
+  out->ns = ns;
+  out->smem = kRingCtlBytes + static_cast<size_t>(ns) * slot + red;
+  return true;
 }
 
 template <int DT, int KC, bool LN, bool DB, int T>
@@ -361,11 +357,7 @@ static int launch_nbr_k(const qb_norm_bwd_args& a, const NbrPlan& plan, int64_t 
 template <int DT, int T>
 static int launch_nbr_dt(const qb_norm_bwd_args& a, const NbrPlan& plan, int64_t clusters,
                          cudaStream_t st) {
-  switch (plan.kc) {
-    case 1: return launch_nbr_k<DT, 1, T>(a, plan, clusters, st);
-    case 2: return launch_nbr_k<DT, 2, T>(a, plan, clusters, st);
-    case 3: return launch_nbr_k<DT, 3, T>(a, plan, clusters, st);
-  }
+  if (plan.kc == 3) return launch_nbr_k<DT, 3, T>(a, plan, clusters, st);
   return QB_ERR_UNSUPPORTED;
 }
 
@@ -374,24 +366,22 @@ static int nbr_resident_clusters(const NbrPlan& plan, const DeviceFacts* dev) {
   if (plan.cluster_n == 1) return dev->sm_count * per_sm;  // shared memory and threads
   // every instantiation has the same footprint class; the plainest one stands for them
   const void* rep = plan.threads == 512
-      ? reinterpret_cast<const void*>(norm_bwd_ring_kernel<QB_BF16, 1, 4, false, false, 512>)
-      : reinterpret_cast<const void*>(norm_bwd_ring_kernel<QB_BF16, 1, 4, false, false, 256>);
+      ? reinterpret_cast<const void*>(norm_bwd_ring_kernel<QB_BF16, 3, 1, false, false, 512>)
+      : reinterpret_cast<const void*>(norm_bwd_ring_kernel<QB_BF16, 3, 1, false, false, 256>);
   const int n = cached_max_clusters(rep, plan.threads, plan.smem, plan.cluster_n);
   return n > 0 ? n : dev->sm_count * per_sm / plan.cluster_n;
 }
 
-// CTA size: 256 threads (two CTAs per SM, whose phases overlap) wherever the row fits that way.
-static bool plan_norm_bwd_ring_any(int64_t N, int x_dtype, int want_threads, int max_smem_optin,
-                                   NbrPlan* out) {
-  if (want_threads == 256 || want_threads == 512)
-    return plan_norm_bwd_ring(N, x_dtype, want_threads, max_smem_optin, out);
-  return plan_norm_bwd_ring(N, x_dtype, 256, max_smem_optin, out) ||
-         plan_norm_bwd_ring(N, x_dtype, 512, max_smem_optin, out);
+// 512 threads (one CTA per SM; clusters of up to 4 for long rows) where the row fits that way,
+// else 256 threads (two CTAs per SM).
+static bool plan_norm_bwd_ring_any(int64_t N, int x_dtype, int max_smem_optin, NbrPlan* out) {
+  return plan_norm_bwd_ring(N, x_dtype, 512, max_smem_optin, out) ||
+         plan_norm_bwd_ring(N, x_dtype, 256, max_smem_optin, out);
 }
 
 int norm_bwd_ring_num_partials(int64_t N, int x_dtype, const DeviceFacts* dev) {
   NbrPlan plan;
-  if (!plan_norm_bwd_ring_any(N, x_dtype, 0, dev->max_smem_optin, &plan)) return 0;
+  if (!plan_norm_bwd_ring_any(N, x_dtype, dev->max_smem_optin, &plan)) return 0;
   return nbr_resident_clusters(plan, dev);
 }
 
@@ -402,7 +392,7 @@ int launch_norm_bwd_ring(const qb_norm_bwd_args& a, int64_t clusters, const Devi
   if ((reinterpret_cast<uintptr_t>(a.dw_partial) | reinterpret_cast<uintptr_t>(a.db_partial)) % 16 != 0)
     return QB_ERR_UNSUPPORTED;
   NbrPlan plan;
-  if (!plan_norm_bwd_ring_any(a.N, a.x_dtype, a.cfg.num_threads, dev->max_smem_optin, &plan))
+  if (!plan_norm_bwd_ring_any(a.N, a.x_dtype, dev->max_smem_optin, &plan))
     return QB_ERR_UNSUPPORTED;
   // More partial slices than resident clusters would run as a second wave.
   if (clusters > nbr_resident_clusters(plan, dev)) return QB_ERR_UNSUPPORTED;

@@ -42,9 +42,11 @@ static int static_scratch(float** out) {
   if (g_scratch_ptr[device] == nullptr) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_static_scratch);
-    if (e != cudaSuccess || p == nullptr)
+    if (e != cudaSuccess)
       return set_error(QB_ERR_CUDA, "norm_bwd_static: cudaGetSymbolAddress on device %d: %s", device,
                        cudaGetErrorString(e));
+    if (p == nullptr)
+      return set_error(QB_ERR_CUDA, "norm_bwd_static: the workspace has no address on device %d", device);
     g_scratch_ptr[device] = static_cast<float*>(p);
   }
   *out = g_scratch_ptr[device];

@@ -321,8 +321,9 @@ norm_fwd_kernel(const NormFwdParams p) {
 }
 
 struct FwdGrid {
-  int max_ctas;  // override of the persistent-grid cap (0 = resident CTAs)
+  int max_ctas;    // override of the persistent-grid cap (0 = resident CTAs)
   int sm_count;
+  int per_sm_cap;  // CTAs per SM beyond which more rows in flight cost bandwidth (0 = no cap)
 };
 
 template <int DT, int VEC, int K, bool RAW, bool LN>
@@ -333,13 +334,16 @@ static int launch_norm_fwd_s(const NormFwdParams& p, FwdGrid grid, int threads, 
   if constexpr (VEC == 8) {
     if (p.stage_params == 2)
       return launch_persistent(norm_fwd_kernel<DT, VEC, K, LN, RAW, 2>, p.num_tiles, heads, threads,
-                               smem, p.cluster_n, grid.max_ctas, grid.sm_count, st, p, name);
+                               smem, p.cluster_n, grid.max_ctas, grid.sm_count, st, p, name,
+                               grid.per_sm_cap);
   }
   if (p.stage_params)
     return launch_persistent(norm_fwd_kernel<DT, VEC, K, LN, RAW, 1>, p.num_tiles, heads,
-                             threads, smem, p.cluster_n, grid.max_ctas, grid.sm_count, st, p, name);
+                             threads, smem, p.cluster_n, grid.max_ctas, grid.sm_count, st, p, name,
+                             grid.per_sm_cap);
   return launch_persistent(norm_fwd_kernel<DT, VEC, K, LN, RAW, 0>, p.num_tiles, heads, threads,
-                           smem, p.cluster_n, grid.max_ctas, grid.sm_count, st, p, name);
+                           smem, p.cluster_n, grid.max_ctas, grid.sm_count, st, p, name,
+                           grid.per_sm_cap);
 }
 
 template <int DT, int VEC, int K, bool RAW>
@@ -462,9 +466,13 @@ extern "C" int qb_norm_fwd(const qb_norm_fwd_args* args, qb_stream_t stream) {
   // Packed rows: 16 chunks per thread (one warp per 4096-element row), CTAs of 256 threads from
   // 6144 elements on (measured: RMSNorm N = 8192 6.0 -> 6.5 TB/s, N = 12288 5.1 -> 6.2,
   // LayerNorm N = 6144 4.2 -> 5.0); fp32-held rows 8 chunks per thread.
-  const int k_target = raw ? 16 : 8;
-  if (int rc = plan_rows("norm_fwd", a.N, vec, caps, pref, k_target, raw && a.N >= 6144 ? 256 : 128,
-                         a.cfg, &plan))
+  // (Exception, re-measured with the grid rule below: a packed RMSNorm row of exactly 8192 elements
+  // runs 6.08 TB/s as one 128-thread CTA of 8 chunks per thread against 5.57 TB/s the other way;
+  // LayerNorm, with its second pass over the registers, keeps 16 chunks: 5.88 against 4.40 TB/s.)
+  const bool one_cta_row = raw && !a.is_layernorm && a.N * host_dtype_bytes(a.x_dtype) == 16384;
+  const int k_target = (raw && !one_cta_row) ? 16 : 8;
+  if (int rc = plan_rows("norm_fwd", a.N, vec, caps, pref, k_target,
+                         raw && a.N >= 6144 && !one_cta_row ? 256 : 128, a.cfg, &plan))
     return rc;
   const int K = plan.K;
   const int threads = plan.threads;
@@ -493,7 +501,16 @@ extern "C" int qb_norm_fwd(const qb_norm_fwd_args* args, qb_stream_t stream) {
   }
   // Persistent grid: exactly the CTAs that are resident at once, each walking over row tiles (so
   // weight / bias are staged once per CTA, not once per row).
-  const FwdGrid grid = {a.cfg.max_ctas, dev->sm_count};
+  // CTAs per SM.  Measured on B200 (bf16): CTAs whose tile holds 32 KB of input rows run best three
+  // to an SM (96 KB of rows in flight), not four -- RMSNorm with a residual at N = 8192: 2 / 3 / 4
+  // CTAs per SM 5.82 / 6.41 / 5.99 TB/s; LayerNorm at N = 4096 (4 rows per CTA): 5.18 / 6.08 /
+  // 5.90 TB/s -- so the persistent grid of such kernels is capped at 96 KB per SM.  Larger tiles
+  // (64 KB: two CTAs per SM) keep everything that fits.
+  const int64_t tile_bytes = static_cast<int64_t>(plan.rows_per_cta) * plan.cols_per_cta *
+                             host_dtype_bytes(a.x_dtype) * (a.residual != nullptr ? 2 : 1);
+  const int per_sm_cap =
+      (tile_bytes > 0 && tile_bytes <= (32 << 10)) ? static_cast<int>((96 << 10) / tile_bytes) : 0;
+  const FwdGrid grid = {a.cfg.max_ctas, dev->sm_count, a.H == 1 ? per_sm_cap : 0};
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
 
   if (uniform) {

@@ -288,12 +288,12 @@ template <int DT, bool BWD>
 static int launch_softmax_ring_dt(const SoftmaxParams& p, const qb_launch_cfg& cfg,
                                   const DeviceFacts* dev, cudaStream_t st) {
   // cfg.num_threads = consumer threads (256 / 512 / 768), cfg.stages = 16-byte chunks per thread
-  // and slot.  Measured on B200 (bf16, 2 GiB per tensor): backward 512 consumers x 2 chunks
-  // (16 KB per input and slot), forward 512 x 4 (32 KB slots: the forward pass is bound by
-  // instruction issue and the special function unit, and larger slots amortise the per-slot
-  // bookkeeping).
-  const int t = cfg.num_threads > 0 ? cfg.num_threads : 512;
-  const int u = cfg.stages > 0 ? cfg.stages : (BWD ? 2 : 4);
+  // and slot.  Measured on B200 (bf16, 2 and 4 GiB per tensor): backward 256 consumers x 4 chunks
+  // (16 KB per input and slot: 6.65 TB/s at N = 65536, 6.08 at 131072, against 6.54 / 5.87 with
+  // 512 x 2), forward 512 x 4 (32 KB slots: the forward pass is bound by instruction issue and
+  // the special function unit, and larger slots amortise the per-slot bookkeeping).
+  const int t = cfg.num_threads > 0 ? cfg.num_threads : (BWD ? 256 : 512);
+  const int u = cfg.stages > 0 ? cfg.stages : 4;
 #define QB_RING_CASE(TT, UU) \
   if (t == TT && u == UU) return launch_softmax_ring_t<DT, BWD, TT, UU>(p, cfg, dev, st);
   QB_RING_CASE(256, 4)

@@ -89,9 +89,97 @@ def _cfg_struct(config, op: str) -> _C.LaunchCfg:
     return _C.make_cfg(config.num_threads, config.threads_per_row, config.cluster_n, 0, stages)
 
 
+_CODES = _C.FLOAT_CODES
+_F32 = torch.float32
+
+
+def _fast_norm_fwd(x, weight, out, bias, rstd, mean, residual, residual_out, eps, is_layernorm,
+                   weight_offset, config) -> bool:
+    """The common case in a few microseconds of host time: 2-D tensors with unit column stride,
+    1-D contiguous parameters, fp32 contiguous statistics, everything valid.  Returns False --
+    having done nothing -- whenever anything is unusual, and the general path below (which also
+    produces the reference's error messages) takes over."""
+    if x.dim() != 2 or not x.is_cuda:
+        return False
+    M, N = x.shape
+    if M == 0 or N == 0:
+        return False
+    xd = _CODES.get(x.dtype)
+    od = _CODES.get(out.dtype)
+    if xd is None or od is None or out.shape != x.shape or not out.is_cuda:
+        return False
+    xs, os_ = x.stride(), out.stride()
+    if xs[1] != 1 or os_[1] != 1:
+        return False
+    a = _C.NormFwdArgs()
+    a.x = x.data_ptr()
+    a.out = out.data_ptr()
+    a.x_row_stride = xs[0]
+    a.out_row_stride = os_[0]
+    a.x_dtype = xd
+    a.out_dtype = od
+    wd = bd = rd = rod = None
+    if weight is not None:
+        wd = _CODES.get(weight.dtype)
+        if wd is None or weight.dim() != 1 or weight.shape[0] != N or not weight.is_contiguous() or not weight.is_cuda:
+            return False
+        a.weight = weight.data_ptr()
+        a.weight_dtype = wd
+    if bias is not None:
+        bd = _CODES.get(bias.dtype)
+        if bd is None or bias.dim() != 1 or bias.shape[0] != N or not bias.is_contiguous() or not bias.is_cuda:
+            return False
+        a.bias = bias.data_ptr()
+        a.bias_dtype = bd
+    if residual is not None:
+        rd = _CODES.get(residual.dtype)
+        rs = residual.stride()
+        if rd is None or residual.shape != x.shape or rs[1] != 1 or not residual.is_cuda:
+            return False
+        a.residual = residual.data_ptr()
+        a.residual_dtype = rd
+        a.residual_row_stride = rs[0]
+    if residual_out is not None:
+        rod = _CODES.get(residual_out.dtype)
+        ros = residual_out.stride()
+        if rod is None or residual_out.shape != x.shape or ros[1] != 1 or not residual_out.is_cuda:
+            return False
+        a.residual_out = residual_out.data_ptr()
+        a.residual_out_dtype = rod
+        a.residual_out_row_stride = ros[0]
+    if rstd is not None:
+        if rstd.dtype != _F32 or rstd.numel() != M or not rstd.is_contiguous() or not rstd.is_cuda:
+            return False
+        a.rstd = rstd.data_ptr()
+    if mean is not None:
+        if mean.dtype != _F32 or mean.numel() != M or not mean.is_contiguous() or not mean.is_cuda:
+            return False
+        a.mean = mean.data_ptr()
+    _compile_rmsnorm_fwd.note((xd, od, rd, wd, bd, rod, N, rstd is not None, mean is not None,
+                               bool(is_layernorm), False, float(weight_offset)))
+    a.M = M
+    a.H = 1
+    a.N = N
+    a.is_layernorm = 1 if is_layernorm else 0
+    a.eps = eps
+    a.weight_offset = weight_offset
+    if config is not None:
+        a.cfg = _cfg_struct(config, "norm_fwd")
+    else:
+        cfg = _C.env_cfg("norm_fwd")
+        if cfg is not None:
+            a.cfg = cfg
+    _C.launch(_C.lib().qb_norm_fwd, a, x, "rmsnorm_fwd")
+    return True
+
+
+
 def _launch_norm_fwd(x, weight, out, bias, rstd, mean, residual, residual_out, eps, is_layernorm,
                      weight_offset, config=None) -> None:
     """Validates like the reference op body + its TVM-FFI call, then enqueues qb_norm_fwd."""
+    if _fast_norm_fwd(x, weight, out, bias, rstd, mean, residual, residual_out, eps, is_layernorm,
+                      weight_offset, config):
+        return
     assert x.dtype in _SUPPORTED, "Unsupported dtype"
     if weight is not None:
         assert weight.dtype in _SUPPORTED, "Weight must be float32, float16 or bfloat16"
@@ -126,11 +214,10 @@ def _launch_norm_fwd(x, weight, out, bias, rstd, mean, residual, residual_out, e
             raise ValueError(f"Mismatched {name}.shape[0] on argument {name}: expected {rows}, got {t.numel()}")
     if x.numel() == 0:
         return
+    code = lambda t: None if t is None else _CODES.get(t.dtype)  # noqa: E731
     _compile_rmsnorm_fwd.note((
-        x.dtype, out.dtype, None if residual is None else residual.dtype,
-        None if weight is None else weight.dtype, None if bias is None else bias.dtype,
-        None if residual_out is None else residual_out.dtype, N, rstd is not None,
-        mean is not None, bool(is_layernorm), per_head, float(weight_offset),
+        code(x), code(out), code(residual), code(weight), code(bias), code(residual_out), N,
+        rstd is not None, mean is not None, bool(is_layernorm), per_head, float(weight_offset),
     ))
     # Inputs are copied if their rows cannot be addressed with one stride; outputs are written in
     # place, through a temporary only in that same (rare) case.
@@ -167,8 +254,7 @@ def _launch_norm_fwd(x, weight, out, bias, rstd, mean, residual, residual_out, e
     a.eps = float(eps)
     a.weight_offset = float(weight_offset)
     a.cfg = _cfg_struct(config, "norm_fwd")
-    with _C.device_of(x_):
-        _C.check(_C.lib().qb_norm_fwd(byref(a), _C.stream_of(x_)), "rmsnorm_fwd")
+    _C.launch(_C.lib().qb_norm_fwd, a, x_, "rmsnorm_fwd")
     for dst, src in ((out, out_), (residual_out, ro_), (rstd, rstd_), (mean, mean_)):
         if dst is not None and dst is not src:
             dst.copy_(src)
@@ -229,8 +315,81 @@ def rmsnorm_fwd(
     return out, (x if residual_out is None else residual_out), rstd
 
 
+def _fast_norm_bwd(x, weight, dout, rstd, dx, dw_partial, db_partial, dresidual_out, dresidual,
+                   sm_count, mean, is_layernorm, weight_offset, config) -> bool:
+    """Lean host path of the common backward call (2-D, unit column strides, no residual-gradient
+    streams, everything valid); returns False without side effects otherwise."""
+    if x.dim() != 2 or dresidual_out is not None or dresidual is not None or not x.is_cuda:
+        return False
+    M, N = x.shape
+    if M == 0 or N == 0 or (mean is not None) != bool(is_layernorm):
+        return False
+    xd, dd, gd = _CODES.get(x.dtype), _CODES.get(dout.dtype), _CODES.get(dx.dtype)
+    if xd is None or dd is None or gd is None or dout.shape != x.shape or dx.shape != x.shape:
+        return False
+    xs, ds, gs = x.stride(), dout.stride(), dx.stride()
+    if xs[1] != 1 or ds[1] != 1 or gs[1] != 1 or not (dout.is_cuda and dx.is_cuda):
+        return False
+    if rstd.dtype != _F32 or rstd.numel() != M or not rstd.is_contiguous() or not rstd.is_cuda:
+        return False
+    a = _C.NormBwdArgs()
+    wd = None
+    if weight is not None:
+        wd = _CODES.get(weight.dtype)
+        if wd is None or weight.dim() != 1 or weight.shape[0] != N or not weight.is_contiguous() or not weight.is_cuda:
+            return False
+        a.weight = weight.data_ptr()
+        a.weight_dtype = wd
+    if mean is not None:
+        if mean.dtype != _F32 or mean.numel() != M or not mean.is_contiguous() or not mean.is_cuda:
+            return False
+        a.mean = mean.data_ptr()
+    if dw_partial is None and db_partial is None:
+        if sm_count is None:
+            return False
+        P = int(sm_count)
+    else:
+        P = dw_partial.shape[0] if dw_partial is not None else db_partial.shape[0]
+    for t in (dw_partial, db_partial):
+        if t is not None and (t.dtype != _F32 or not t.is_contiguous() or t.numel() != P * N or not t.is_cuda):
+            return False
+    _compile_rmsnorm_bwd.note((N, xd, dd, gd, wd, db_partial is not None, None, None,
+                               dw_partial is not None, False, bool(is_layernorm), float(weight_offset)))
+    a.x = x.data_ptr()
+    a.dout = dout.data_ptr()
+    a.rstd = rstd.data_ptr()
+    a.dx = dx.data_ptr()
+    if dw_partial is not None:
+        a.dw_partial = dw_partial.data_ptr()
+    if db_partial is not None:
+        a.db_partial = db_partial.data_ptr()
+    a.M = M
+    a.H = 1
+    a.N = N
+    a.x_row_stride = xs[0]
+    a.dout_row_stride = ds[0]
+    a.dx_row_stride = gs[0]
+    a.num_partials = P
+    a.x_dtype = xd
+    a.dout_dtype = dd
+    a.dx_dtype = gd
+    a.is_layernorm = 1 if is_layernorm else 0
+    a.weight_offset = weight_offset
+    if config is not None:
+        a.cfg = _cfg_struct(config, "norm_bwd")
+    else:
+        cfg = _C.env_cfg("norm_bwd")
+        if cfg is not None:
+            a.cfg = cfg
+    _C.launch(_C.lib().qb_norm_bwd, a, x, "rmsnorm_bwd")
+    return True
+
+
 def _launch_norm_bwd(x, weight, dout, rstd, dx, dw_partial, db_partial, dresidual_out, dresidual,
                      sm_count, mean, is_layernorm, weight_offset, config=None) -> None:
+    if _fast_norm_bwd(x, weight, dout, rstd, dx, dw_partial, db_partial, dresidual_out, dresidual,
+                      sm_count, mean, is_layernorm, weight_offset, config):
+        return
     assert x.dim() in (2, 3), "Input must be 2D or 3D"
     assert x.dtype in _SUPPORTED, "Unsupported dtype"
     assert (mean is not None) == bool(is_layernorm), "mean is required iff is_layernorm"
@@ -268,11 +427,10 @@ def _launch_norm_bwd(x, weight, dout, rstd, dx, dw_partial, db_partial, dresidua
         if t is not None:
             assert t.dtype == torch.float32 and t.is_contiguous(), "partials must be contiguous fp32"
             assert t.numel() == P * H * N, "partial workspace must be (sm_count, [H,] N)"
+    code = lambda t: None if t is None else _CODES.get(t.dtype)  # noqa: E731
     _compile_rmsnorm_bwd.note((
-        N, x.dtype, dout.dtype, dx.dtype, None if weight is None else weight.dtype,
-        db_partial is not None, None if dresidual is None else dresidual.dtype,
-        None if dresidual_out is None else dresidual_out.dtype, dw_partial is not None, per_head,
-        bool(is_layernorm), float(weight_offset),
+        N, code(x), code(dout), code(dx), code(weight), db_partial is not None, code(dresidual),
+        code(dresidual_out), dw_partial is not None, per_head, bool(is_layernorm), float(weight_offset),
     ))
     x_ = x if _row_stride(x) is not None else x.contiguous()
     dout_ = dout if _row_stride(dout) is not None else dout.contiguous()
@@ -310,8 +468,7 @@ def _launch_norm_bwd(x, weight, dout, rstd, dx, dw_partial, db_partial, dresidua
     a.is_layernorm = int(bool(is_layernorm))
     a.weight_offset = float(weight_offset)
     a.cfg = _cfg_struct(config, "norm_bwd")
-    with _C.device_of(x_):
-        _C.check(_C.lib().qb_norm_bwd(byref(a), _C.stream_of(x_)), "rmsnorm_bwd")
+    _C.launch(_C.lib().qb_norm_bwd, a, x_, "rmsnorm_bwd")
     for dst, src in ((dx, dx_), (dresidual, dr_)):
         if dst is not None and dst is not src:
             dst.copy_(src)
@@ -361,8 +518,7 @@ def _norm_bwd_colsum(partial: Tensor, out: Tensor) -> None:
     a.P = partial.shape[0]
     a.cols = out.numel()
     a.out_dtype = _C.float_code(out)
-    with _C.device_of(partial):
-        _C.check(_C.lib().qb_colsum(byref(a), _C.stream_of(partial)), "norm_bwd_colsum")
+    _C.launch(_C.lib().qb_colsum, a, partial, "norm_bwd_colsum")
 
 
 def _finalize_partials(partial: Tensor, dtype: torch.dtype) -> Tensor:

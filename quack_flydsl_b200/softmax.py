@@ -27,8 +27,9 @@ def _softmax_fwd(x: torch.Tensor, out: torch.Tensor) -> None:
     assert x.dim() == 2, "Input must be 2D"
     assert x.dtype in _SUPPORTED, "Unsupported dtype"
     assert out.shape == x.shape and out.dtype in _SUPPORTED
-    _C.require_cuda(x, "mX")
-    _C.require_cuda(out, "mO")
+    if not (x.is_cuda and out.is_cuda):
+        _C.require_cuda(x, "mX")
+        _C.require_cuda(out, "mO")
     if x.numel() == 0:
         return
     x_ = _rows(x)
@@ -38,9 +39,10 @@ def _softmax_fwd(x: torch.Tensor, out: torch.Tensor) -> None:
     a.M, a.N = x_.shape
     a.x_row_stride, a.out_row_stride = x_.stride(0), out_.stride(0)
     a.x_dtype, a.out_dtype = _C.float_code(x_), _C.float_code(out_)
-    a.cfg = _C.env_cfg("softmax_fwd") or _C.make_cfg()
-    with _C.device_of(x_):
-        _C.check(_C.lib().qb_softmax_fwd(byref(a), _C.stream_of(x_)), "softmax_fwd")
+    cfg = _C.env_cfg("softmax_fwd")
+    if cfg is not None:
+        a.cfg = cfg
+    _C.launch(_C.lib().qb_softmax_fwd, a, x_, "softmax_fwd")
     if out_ is not out:
         out.copy_(out_)
 
@@ -60,8 +62,9 @@ def _softmax_backward(dy: torch.Tensor, y: torch.Tensor, dx: torch.Tensor) -> No
     assert dy.dtype in _SUPPORTED, "Unsupported dtype"
     assert y.dtype == dy.dtype, "dy and y must have same dtype"
     assert dx.shape == dy.shape and dx.dtype in _SUPPORTED
-    for name, t in (("mdY", dy), ("mY", y), ("mdX", dx)):
-        _C.require_cuda(t, name)
+    if not (dy.is_cuda and y.is_cuda and dx.is_cuda):
+        for name, t in (("mdY", dy), ("mY", y), ("mdX", dx)):
+            _C.require_cuda(t, name)
     if dy.numel() == 0:
         return
     dy_, y_ = _rows(dy), _rows(y)
@@ -71,9 +74,10 @@ def _softmax_backward(dy: torch.Tensor, y: torch.Tensor, dx: torch.Tensor) -> No
     a.M, a.N = dy_.shape
     a.dy_row_stride, a.y_row_stride, a.dx_row_stride = dy_.stride(0), y_.stride(0), dx_.stride(0)
     a.dy_dtype, a.y_dtype, a.dx_dtype = _C.float_code(dy_), _C.float_code(y_), _C.float_code(dx_)
-    a.cfg = _C.env_cfg("softmax_bwd") or _C.make_cfg()
-    with _C.device_of(dy_):
-        _C.check(_C.lib().qb_softmax_bwd(byref(a), _C.stream_of(dy_)), "softmax_bwd")
+    cfg = _C.env_cfg("softmax_bwd")
+    if cfg is not None:
+        a.cfg = cfg
+    _C.launch(_C.lib().qb_softmax_bwd, a, dy_, "softmax_bwd")
     if dx_ is not dx:
         dx.copy_(dx_)
 

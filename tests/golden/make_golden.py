@@ -17,6 +17,9 @@ What is executed:
   run with autograd on CPU (fp32 upcast, as tests/test_linear_cross_entropy.py:33-35 does), and
   the closed form the reference's ``rms_final_reduce`` test compares with
   (tests/test_linear.py:793-803).
+* ``torch.topk`` (largest, sorted) + ``torch.softmax`` over the k values + autograd, the ground
+  truth of the reference's top-k test (tests/test_topk.py:40-80); needs no reference checkout:
+  ``python tests/golden/make_golden.py --only topk``.
 Inputs are stored next to the outputs, so the fixtures do not depend on RNG reproducibility.
 """
 
@@ -181,12 +184,39 @@ def gen_linear_ce(ref_root: Path) -> dict:
     return {"linear_cross_entropy": cases, "rms_final_reduce": rms}
 
 
+def gen_topk() -> dict:
+    g = torch.Generator().manual_seed(4)
+    cases = []
+    for M, N, k, dt, softmax in [
+        (5, 64, 16, torch.float32, False), (3, 128, 32, torch.bfloat16, True),
+        (4, 256, 16, torch.float16, False), (2, 1024, 32, torch.bfloat16, False),
+        (3, 4096, 128, torch.bfloat16, True), (2, 4096, 64, torch.float32, True),
+        (3, 2048, 8, torch.float32, False), (6, 32, 1, torch.float16, True),
+    ]:
+        x = torch.randn(M, N, generator=g).to(dt).requires_grad_()
+        vals, idx = torch.topk(x, k, dim=-1, largest=True, sorted=True)
+        out = torch.softmax(vals.float(), dim=-1).to(dt) if softmax else vals
+        dvalues = torch.randn(M, k, generator=g).to(dt)
+        (dx,) = torch.autograd.grad(out, x, dvalues)
+        cases.append(dict(x=x.detach(), k=k, softmax=softmax, values=out.detach(), indices=idx.to(torch.int32),
+                          dvalues=dvalues, dx=dx))
+    return {"topk": cases}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", required=True, help="root of the reference project checkout")
+    ap.add_argument("--only", default=None, help="regenerate one fixture file only (topk)")
+    ap.add_argument("--reference", default=None, help="root of the reference project checkout")
     args = ap.parse_args()
     torch.manual_seed(0)
     torch.set_num_threads(1)  # fixed summation order in the generating run
+    if args.only in (None, "topk"):
+        torch.save(gen_topk(), HERE / "topk_golden.pt")
+        print("topk_golden.pt", (HERE / "topk_golden.pt").stat().st_size, "bytes")
+    if args.only == "topk":
+        return
+    if args.reference is None:
+        ap.error("--reference is required for everything but --only topk")
     ref = load_reference_functions(Path(args.reference))
     torch.save({**gen_norm(ref), **gen_layernorm(ref)}, HERE / "norm_golden.pt")
     torch.save({**gen_softmax(), **gen_cross_entropy()}, HERE / "softmax_ce_golden.pt")

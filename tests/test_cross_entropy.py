@@ -53,7 +53,7 @@ def test_cross_entropy(M, N, dtype, has_weight):
 
 
 def test_cross_entropy_config_shape_fp32_outputs():
-    """BASELINE configuration shape family (bf16 logits = 2 * N(0,1), N = 128256, int64 targets, 5 %
+    """Benchmark shape family (bf16 logits = 2 * N(0,1), N = 128256, int64 targets, 5 %
     ignored, mean reduction) on a row slice the CPU oracle handles; loss and lse to rtol 1e-5."""
     M = 512
     d = oracle.make_config_inputs("c5", rows=M, device=DEV)

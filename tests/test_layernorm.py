@@ -94,7 +94,7 @@ def test_layernorm_golden_fixtures(norm_golden):
 
 
 def test_layernorm_autograd_bf16_params_config_shape():
-    """Shape family of the BASELINE LayerNorm configuration (bf16 x, weight and bias, eps 1e-5,
+    """Shape family of the LayerNorm benchmark configuration (bf16 x, weight and bias, eps 1e-5,
     x ~ N(0.5, 1)) through the autograd wrapper, on a row slice the CPU oracle handles."""
     M, N, eps = 2048, 4096, 1e-5
     d = oracle.make_config_inputs("c3", rows=M, device=DEV)
@@ -115,7 +115,7 @@ def test_layernorm_autograd_bf16_params_config_shape():
 
 
 def test_layernorm_full_size_config_properties():
-    """BASELINE configuration bf16 [65536, 4096] at full size: statistics against the fp32 formulas
+    """Benchmark shape bf16 [65536, 4096] at full size: statistics against the fp32 formulas
     on the GPU, outputs through size-independent properties."""
     M, N, eps = 65536, 4096, 1e-5
     g = torch.Generator(device=DEV).manual_seed(0)

@@ -322,7 +322,7 @@ def test_rmsnorm_backward_is_bitwise_deterministic():
 
 
 def test_rmsnorm_full_size_config_roundtrip_properties():
-    """BASELINE configuration (bf16 [32768, 8192] + residual) at full size: checked through
+    """Headline benchmark shape (bf16 [32768, 8192] + residual) at full size: checked through
     size-independent properties and against the fp32 formulas evaluated on the GPU."""
     M, N = 32768, 8192
     g = torch.Generator(device=DEV).manual_seed(0)

@@ -1,5 +1,5 @@
 """GPU parity tests of softmax forward / backward against the CPU oracle, after the reference's
-tests/test_softmax.py, plus the BASELINE row sweep (N = 4096 ... 131072) at reduced M."""
+tests/test_softmax.py, plus the benchmark row sweep (N = 4096 ... 131072) at reduced M."""
 
 import importlib
 
@@ -36,7 +36,7 @@ def test_softmax(M, N, dtype):
 
 @pytest.mark.parametrize("N", [4096, 16384, 65536, 131072])
 def test_softmax_config_row_sweep(N):
-    """BASELINE softmax sweep (x = 3 * N(0,1) bf16, dy ~ N(0,1)) at reduced M."""
+    """Benchmark softmax sweep (x = 3 * N(0,1) bf16, dy ~ N(0,1)) at reduced M."""
     M = 2 ** 24 // N
     d = oracle.make_config_inputs(f"c4:{N}", rows=M, device=DEV)
     y = sm.softmax_fwd(d["x"])

@@ -11,6 +11,7 @@ from ctypes import byref
 import pytest
 import torch
 
+import oracle
 from quack_flydsl_b200 import _C
 
 pytestmark = pytest.mark.gpu
@@ -172,3 +173,101 @@ def test_static_workspace_rejects_rows_beyond_its_capacity():
     torch.cuda.synchronize()
     assert torch.equal(dx, dx_ref)
     _assert_param_grad_close(dw, dw_ref, 8)
+
+
+def test_static_workspace_against_the_cpu_oracle():
+    """Not only against the stock CUDA entry points: dx, dw and db of the no-allocation entry point
+    against the CPU oracle's LayerNorm backward on the same inputs."""
+    M, N = 1500, 2048
+    x, w, dout, rstd, mean = _inputs(M, N, torch.bfloat16, True, seed=11)
+    for call in range(2):
+        rc, dx, dw, db = _static(x, w, dout, rstd, mean, True, True)
+        assert rc == 0, _C.lib().qb_last_error().decode()
+        torch.cuda.synchronize()
+        dx_ref, dw_ref, db_ref = oracle.layernorm_bwd_ref(x.cpu(), w.cpu(), dout.cpu(), rstd.cpu(), mean.cpu())
+        scale = float(dx_ref.abs().max())
+        assert (dx.float().cpu() - dx_ref).abs().max().item() <= 2.0**-7 * scale
+        # fp32 parameter gradients: fp32 accumulation over M rows on both sides
+        assert (dw.cpu() - dw_ref).abs().max().item() <= 5e-6 * M**0.5 * max(1.0, float(dw_ref.abs().max()))
+        assert (db.cpu() - db_ref).abs().max().item() <= 5e-6 * M**0.5 * max(1.0, float(db_ref.abs().max()))
+
+
+def test_static_workspace_per_head_and_bias_only():
+    """H > 1 (one weight row per head: the partial slices are (P, H, N)) and a call that wants db
+    but not dw."""
+    M, H, N = 333, 4, 256
+    g = torch.Generator(device="cuda").manual_seed(21)
+    x = torch.randn(M, H, N, device="cuda", generator=g).to(torch.bfloat16)
+    dout = torch.randn(M, H, N, device="cuda", generator=g).to(torch.bfloat16)
+    w = 1 + 0.1 * torch.randn(H, N, device="cuda", generator=g)
+    rstd = torch.rsqrt(x.float().square().mean(dim=-1) + 1e-6)  # (M, H)
+
+    def call(want_dw, want_db):
+        dx = torch.empty_like(x)
+        dw = torch.empty(H, N, device="cuda") if want_dw else None
+        db = torch.empty(H, N, device="cuda") if want_db else None
+        s = _C.NormBwdStaticArgs()
+        a = s.bwd
+        a.x, a.weight, a.dout, a.rstd, a.dx = _C.ptr(x), _C.ptr(w if want_dw else None), _C.ptr(dout), _C.ptr(rstd), _C.ptr(dx)
+        a.M, a.H, a.N = M, H, N
+        a.x_row_stride = a.dout_row_stride = a.dx_row_stride = N
+        a.x_dtype = a.dout_dtype = a.dx_dtype = _C.float_code(x)
+        a.weight_dtype = _C.float_code(w)
+        s.dw, s.db, s.param_dtype = _C.ptr(dw), _C.ptr(db), _C.QB_F32
+        rc = _C.lib().qb_norm_bwd_static(byref(s), _C.stream_of(x))
+        assert rc == 0, _C.lib().qb_last_error().decode()
+        torch.cuda.synchronize()
+        return dx, dw, db
+
+    for _ in range(2):
+        dx, dw, db = call(True, True)
+        xhat = x.float() * rstd[..., None]
+        dw_ref = (dout.float() * xhat).sum(0)
+        db_ref = dout.float().sum(0)
+        torch.testing.assert_close(dw, dw_ref, atol=2e-3, rtol=1e-4)
+        torch.testing.assert_close(db, db_ref, atol=2e-3, rtol=1e-4)
+        wdy = dout.float() * w
+        dx_ref = (wdy - xhat * (xhat * wdy).mean(-1, keepdim=True)) * rstd[..., None]
+        assert (dx.float() - dx_ref).abs().max().item() <= 2.0**-7 * float(dx_ref.abs().max())
+        _, dw2, db2 = call(False, True)
+        assert dw2 is None
+        torch.testing.assert_close(db2, db_ref, atol=2e-3, rtol=1e-4)
+
+
+def test_static_workspace_residual_gradient_and_empty_batch():
+    """The residual-gradient streams (dresidual_out added into dx, dresidual written in its own
+    dtype) and M == 0, where dw / db must come back as zeros without touching the workspace."""
+    M, N = 257, 1024
+    x, w, dout, rstd, _ = _inputs(M, N, torch.bfloat16, False, seed=31)
+    dres_out = torch.randn(M, N, device="cuda")  # fp32 residual stream
+    dx = torch.empty_like(x)
+    dres = torch.empty_like(dres_out)
+    dw = torch.empty(N, device="cuda")
+    s = _C.NormBwdStaticArgs()
+    _fill_bwd(s.bwd, x, w, dout, rstd, None, dx, False)
+    s.bwd.dresidual_out, s.bwd.dresidual = _C.ptr(dres_out), _C.ptr(dres)
+    s.bwd.dresidual_out_row_stride = s.bwd.dresidual_row_stride = N
+    s.bwd.dresidual_out_dtype = s.bwd.dresidual_dtype = _C.QB_F32
+    s.dw, s.db, s.param_dtype = _C.ptr(dw), None, _C.QB_F32
+    for _ in range(2):
+        assert _C.lib().qb_norm_bwd_static(byref(s), _C.stream_of(x)) == 0, _C.lib().qb_last_error().decode()
+        torch.cuda.synchronize()
+        xhat = x.float() * rstd[:, None]
+        wdy = dout.float() * w
+        ref = (wdy - xhat * (xhat * wdy).mean(-1, keepdim=True)) * rstd[:, None] + dres_out
+        torch.testing.assert_close(dres, ref, atol=1e-4, rtol=1e-4)
+        assert (dx.float() - ref).abs().max().item() <= 2.0**-7 * float(ref.abs().max())
+        torch.testing.assert_close(dw, (dout.float() * xhat).sum(0), atol=2e-3, rtol=1e-4)
+    # empty batch
+    e = torch.empty(0, N, device="cuda", dtype=torch.bfloat16)
+    dw.fill_(7.0)
+    db = torch.full((N,), 7.0, device="cuda")
+    s2 = _C.NormBwdStaticArgs()
+    _fill_bwd(s2.bwd, e, w, e, rstd[:0], None, e, False)
+    s2.dw, s2.db, s2.param_dtype = _C.ptr(dw), _C.ptr(db), _C.QB_F32
+    # data_ptr() of an empty tensor is 0: give the entry point non-null dummies for the row tensors
+    s2.bwd.x = s2.bwd.dout = s2.bwd.dx = _C.ptr(x)
+    s2.bwd.rstd = _C.ptr(rstd)
+    assert _C.lib().qb_norm_bwd_static(byref(s2), _C.stream_of(x)) == 0, _C.lib().qb_last_error().decode()
+    torch.cuda.synchronize()
+    assert (dw == 0).all() and (db == 0).all()
