@@ -643,13 +643,13 @@ def _rmsnorm_bwd_tuned(
     dout: Tensor,
     rstd: Tensor,
     dx: Tensor,
-    dw_partial: Optional[Tensor],
+    dw_partial: Optional[Tensor] = None,
     db_partial: Optional[Tensor] = None,
     dresidual_out: Optional[Tensor] = None,
     dresidual: Optional[Tensor] = None,
     sm_count: Optional[int] = None,
     per_head: bool = False,
-    has_dw_partial: bool = True,
+    has_dw_partial: bool = False,
     has_db_partial: bool = False,
     mean: Optional[Tensor] = None,
     is_layernorm: bool = False,
@@ -660,6 +660,13 @@ def _rmsnorm_bwd_tuned(
         raise RuntimeError(
             "rmsnorm_bwd_tuned requires a config (provided automatically when the tuned object "
             "is called). Use rmsnorm_bwd for the un-tuned path."
+        )
+    # The persistent grid is the leading extent of the partial-sum buffers; without them the
+    # caller has to say how many CTAs to use (reference: quack/rmsnorm.py:1450-1461).
+    if dw_partial is None and db_partial is None and sm_count is None:
+        raise ValueError(
+            "rmsnorm_bwd_tuned: sm_count is required when neither dw_partial "
+            "nor db_partial is provided."
         )
     _launch_norm_bwd(x, weight, dout, rstd, dx, dw_partial, db_partial, dresidual_out, dresidual,
                      sm_count, mean, is_layernorm, weight_offset, config=config)
