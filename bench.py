@@ -479,13 +479,19 @@ def sharded_suite(dev, rank, world, peak) -> dict:
     grads32 = torch.empty(2, N, device=dev)
     grads = torch.empty(2, N, device=dev, dtype=bf)
 
-    def ln_step(tl=None):
+    peer = sharded.PeerAllReduce(dev, cap_cols=2 * N)
+
+    def ln_step(tl=None, fused=True):
         run = tl.run if tl is not None else (lambda _n, f: f())
         run("fwd", lambda: rn._rmsnorm_fwd(xs, w, out, b, rstd, mean, None, None, 1e-5, True))
         run("bwd", lambda: rn._rmsnorm_bwd(xs, w, ds, rstd, dxs, dwp, dbp, None, None, P, mean, True))
-        run("colsum", lambda: (rn._norm_bwd_colsum(dwp, grads32[0]), rn._norm_bwd_colsum(dbp, grads32[1])))
-        run("allreduce", lambda: dist.all_reduce(grads32))
-        run("round", lambda: grads.copy_(grads32))
+        if fused:
+            run("colsum_allreduce", lambda: peer.reduce([dwp, dbp], outs=[grads[0], grads[1]],
+                                                        outs_f32=[grads32[0], grads32[1]]))
+        else:
+            run("colsum", lambda: (rn._norm_bwd_colsum(dwp, grads32[0]), rn._norm_bwd_colsum(dbp, grads32[1])))
+            run("allreduce", lambda: dist.all_reduce(grads32))
+            run("round", lambda: grads.copy_(grads32))
 
     ln_step()
     # check: rank 0 recomputes dw / db on all rows, unsharded
@@ -514,11 +520,29 @@ def sharded_suite(dev, rank, world, peak) -> dict:
     torch.cuda.synchronize()
     ms = max_ms(e0.elapsed_time(e1) / 20)
     phases = {k: round(max_ms(v), 4) for k, v in tl.median_ms().items()}
+    # the same step with the two-step exchange (column sums, NCCL all-reduce, rounding), for comparison
+    tl2 = Timeline()
+    for _ in range(3):
+        ln_step(fused=False)
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(20):
+        ln_step(tl2, fused=False)
+    e1.record()
+    torch.cuda.synchronize()
+    ms_nccl = max_ms(e0.elapsed_time(e1) / 20)
+    phases_nccl = {k: round(max_ms(v), 4) for k, v in tl2.median_ms().items()}
     nbytes = ln_fwd_bytes(M, N) + ln_bwd_bytes(M, N)
     res["layernorm_row_sharded"] = {
         "shape": [M, N], "rows_per_rank": Ms, "ms": round(ms, 4), "gbs_aggregate": round(nbytes / ms / 1e6, 1),
         "frac_of_measured_peak": round(nbytes / ms / 1e6 / (peak * world), 4), "phases_ms": phases,
-        "collective": "one NCCL all-reduce of fp32 [dw | db] (32 KiB)", "self_check": ok_ln}
+        "collective": "fp32 [dw | db] summed over the GPUs inside the stage-2 kernel (peer stores + flags)",
+        "collective_timeouts": peer.timeouts(),
+        "with_nccl_allreduce": {"ms": round(ms_nccl, 4), "phases_ms": phases_nccl},
+        "self_check": ok_ln}
+    peer.close()
     del x, dout, xs, ds, out, dxs
 
     # ---- cross-entropy, vocabulary sharded ----
@@ -697,13 +721,23 @@ def run_ours(args) -> None:
     out, res_out, dx = torch.empty_like(x), torch.empty_like(x), torch.empty_like(x)
     rstd = torch.empty(M, device=dev)
     P = get_sm_count(N, dev, bf)
-    dw_partial = torch.empty(P, N, device=dev)
-    # The fp32 column sums go straight into the all-reduce buffer; two buffers alternate so that the
-    # all-reduce of step i (side stream) overlaps the forward of step i + 1.
+    # Two sets of buffers alternate so that the cross-GPU sum of step i (side stream) overlaps the
+    # forward of step i + 1: the partial slices (read by the fused kernel) and the fp32 column sums
+    # (which go straight into the NCCL all-reduce in the two-step form).
+    dw_partials = [torch.empty(P, N, device=dev) for _ in range(2 if world > 1 else 1)]
+    dw_partial = dw_partials[0]
     dw32 = [torch.empty(N, device=dev) for _ in range(2)]
     dw = torch.empty(N, device=dev, dtype=bf)
     tl = Timeline()
-    s_ar = torch.cuda.Stream(device=dev) if world > 1 else None
+    # N > 1: stage 2 and the cross-GPU sum of dw run as ONE kernel over peer-mapped exchange buffers
+    # (qb_colsum_allreduce); --collective nccl selects the two-step form instead (column sum, then an
+    # NCCL all-reduce on a side stream that overlaps the next step's forward).
+    use_peer = world > 1 and args.collective == "peer"
+    peer = None
+    if use_peer:
+        from quack_flydsl_b200 import sharded as _sharded
+        peer = _sharded.PeerAllReduce(dev, cap_cols=N)
+    s_ar = torch.cuda.Stream(device=dev) if (world > 1 and args.collective != "none") else None
     ar_done = [None, None]
     counter = {"i": 0}
 
@@ -711,8 +745,24 @@ def run_ours(args) -> None:
         run = tl.run if record else (lambda _n, f: f())
         xs, rs, os_, ros, dxs, dos = x[:rows], res[:rows], out[:rows], res_out[:rows], dx[:rows], dout[:rows]
         run("rmsnorm_fwd", lambda: rn._rmsnorm_fwd(xs, w, os_, None, rstd[:rows], None, rs, ros, EPS))
+        if use_peer:
+            i = counter["i"] & 1
+            counter["i"] += 1
+            cur = torch.cuda.current_stream(dev)
+            if ar_done[i] is not None:
+                cur.wait_event(ar_done[i])  # this set's previous reduction (two steps ago)
+            run("rmsnorm_bwd", lambda: rn._rmsnorm_bwd(ros, w, dos, rstd[:rows], dxs, dw_partials[i], None, None, None, P))
+            ev = torch.cuda.Event()
+            ev.record(cur)
+            with torch.cuda.stream(s_ar):
+                s_ar.wait_event(ev)
+                run("dw_colsum", lambda: peer.reduce([dw_partials[i]], outs=[dw]))
+                done = torch.cuda.Event()
+                done.record(s_ar)
+            ar_done[i] = done
+            return
         run("rmsnorm_bwd", lambda: rn._rmsnorm_bwd(ros, w, dos, rstd[:rows], dxs, dw_partial, None, None, None, P))
-        if world > 1:
+        if world > 1 and args.collective != "none":
             i = counter["i"] & 1
             counter["i"] += 1
             cur = torch.cuda.current_stream(dev)
@@ -966,8 +1016,16 @@ def run_ours(args) -> None:
         cfg = config_dict()
         cfg.update({"step": "rmsnorm_fwd kernel + rmsnorm_bwd kernel + dw column-sum kernel"
                             + (" + NCCL all-reduce of fp32 dw on a side stream, overlapping the next "
-                               "step's forward" if world > 1 else ""),
+                               "step's forward" if (world > 1 and not use_peer) else ""),
                     "num_partials": P})
+        if use_peer:
+            cfg["step"] = ("rmsnorm_fwd kernel + rmsnorm_bwd kernel + one kernel that sums dw over the partial "
+                           "slices and over the GPUs (plain stores into peer-mapped buffers, flags, bounded waits) "
+                           "on a side stream, overlapping the next step's forward")
+            cfg["collective"] = "peer stores (qb_colsum_allreduce)"
+            cfg["collective_timeouts"] = peer.timeouts()
+        elif world > 1:
+            cfg["collective"] = "NCCL all-reduce"
         mhz = clocks.get("sm_mhz") if clocks else None
         line = {
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -993,6 +1051,8 @@ def run_ours(args) -> None:
             "kernels": kernels,
         }
         print(json.dumps(line), flush=True)
+    if peer is not None:
+        peer.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -1007,6 +1067,8 @@ def main():
     ap.add_argument("--no-suite", action="store_true", help="skip the per-kernel sweep of the other configurations")
     ap.add_argument("--no-e2e", action="store_true",
                     help="skip the end-to-end leg (for profiler launch lists of the timed step alone)")
+    ap.add_argument("--collective", default="peer", choices=["peer", "nccl", "none"],
+                    help="N > 1: how dw is summed over the GPUs (fused peer-store kernel, or column sum + NCCL)")
     ap.add_argument("--only", default=None, help="run one kernel on a small case (for ncu captures)")
     ap.add_argument("--rows", type=int, default=0)
     ap.add_argument("--cols", type=int, default=0)

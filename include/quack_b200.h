@@ -23,7 +23,7 @@
 extern "C" {
 #endif
 
-#define QB_ABI_VERSION 2
+#define QB_ABI_VERSION 3
 
 /* element types of streamed tensors */
 enum qb_dtype { QB_F32 = 0, QB_F16 = 1, QB_BF16 = 2 };
@@ -65,8 +65,9 @@ typedef struct qb_launch_cfg {
 #define QB_FLAG_L2_PLAIN_1 4   /* two-pass kernels that re-read from L2: plain L2 policy, pass 1 */
 #define QB_FLAG_L2_PLAIN_2 8   /* ... and pass 2 */
 #define QB_FLAG_FORCE_TWO_PASS 16 /* two-pass kernel for any row length */
-#define QB_FLAG_NO_RING 32     /* long rows: re-read from L2 instead of the shared-memory ring */
-#define QB_FLAG_RING_FWD 64    /* softmax forward, long rows: the shared-memory ring kernel */
+#define QB_FLAG_NO_RING 32     /* long rows: the two-pass kernel that re-reads the row from L2 */
+#define QB_FLAG_RING 64        /* softmax, long rows: the shared-memory ring kernel */
+#define QB_FLAG_CLUSTER_REGS 128 /* softmax, long rows: register-resident slices over a cluster */
 
 /* Device facts the host side needs for workspace sizing. */
 typedef struct qb_device_info {
@@ -194,6 +195,59 @@ typedef struct qb_colsum_args {
 } qb_colsum_args;
 
 int qb_colsum(const qb_colsum_args* args, qb_stream_t stream);
+
+/*
+ * Stage 2 fused with the cross-GPU sum: out[c] = sum over ranks of sum_p partial[p, c], for the
+ * row-sharded norm backward on the GPUs of one node (one process per GPU).  One launch replaces
+ * qb_colsum + an all-reduce of the fp32 vector: every block stores its column sums into its slot
+ * of every rank's exchange buffer (plain stores to peer-mapped memory), raises a flag there,
+ * waits -- with a time limit -- for the same block's flags from all ranks and adds the slots in
+ * rank order, so all ranks obtain bit-identical gradients.  Up to two partial buffers of the same
+ * shape (dw and db) are reduced by the same launch.  No counterpart in the reference, which has
+ * no multi-GPU path for these operators (its dw / db reduction is quack/rmsnorm.py:1398-1399).
+ *
+ * Exchange buffers: every rank calls qb_peer_buffer_create (cudaMalloc + zero fill + CUDA IPC
+ * handle; the only entry point of this library that allocates device memory), the
+ * QB_PEER_HANDLE_BYTES handles are exchanged by the caller (e.g. torch.distributed
+ * all_gather_object), and every rank maps the others' buffers with qb_peer_buffer_open.
+ * peers[r] is rank r's buffer as seen from the calling process (peers[rank] the local one).
+ * cap_cols (a multiple of 32, the same on all ranks) bounds cols * num_buffers; at most 32768
+ * columns are exchanged per launch (all blocks must be resident together), more returns
+ * QB_ERR_UNSUPPORTED.  seq is the caller's step counter: 1 for the first call on a set of
+ * buffers, then incremented by exactly one per call, the same on every rank.  Calls on one set of
+ * buffers must not overlap.  status (optional, device memory) counts the waits that gave up after
+ * two seconds; it stays 0 in a healthy job.
+ */
+#define QB_MAX_PEERS 8
+#define QB_PEER_HANDLE_BYTES 64
+
+typedef struct qb_colsum_allreduce_args {
+  const float* partial0; /* [P, cols] fp32 */
+  const float* partial1; /* second buffer of the same shape, or NULL */
+  void* out0;            /* [cols] in out_dtype, or NULL */
+  void* out1;
+  float* out0_f32;       /* [cols] fp32, or NULL */
+  float* out1_f32;
+  void* peers[QB_MAX_PEERS];
+  uint32_t* status;
+  int64_t P;
+  int64_t cols;
+  int64_t cap_cols;
+  int32_t num_buffers;   /* 1 or 2 */
+  int32_t out_dtype;
+  int32_t world;
+  int32_t rank;
+  uint32_t seq;
+  int32_t pad0;
+} qb_colsum_allreduce_args;
+
+int qb_colsum_allreduce(const qb_colsum_allreduce_args* args, qb_stream_t stream);
+/* Bytes of one rank's exchange buffer for `world` ranks and cap_cols columns (-1: bad arguments). */
+int64_t qb_peer_buffer_bytes(int32_t world, int64_t cap_cols);
+int qb_peer_buffer_create(int32_t world, int64_t cap_cols, void** local, unsigned char* handle);
+int qb_peer_buffer_open(const unsigned char* handle, void** peer);
+int qb_peer_buffer_close(void* peer);
+int qb_peer_buffer_destroy(void* local);
 
 /*
  * Softmax forward over the last dimension of an (M, N) matrix.
@@ -472,7 +526,7 @@ int qb_abi_version(void);
  * sizeof() of an argument block as compiled into the library, so a foreign-language binding can
  * verify its struct layout before the first call.  which: 0 launch_cfg, 1 norm_fwd, 2 norm_bwd,
  * 3 colsum, 4 softmax_fwd, 5 softmax_bwd, 6 ce_fwd, 7 ce_bwd, 8 ce_combine, 9 device_info,
- * 10 norm_bwd_static, 11 rms_final_reduce, 12 topk_fwd, 13 topk_bwd.
+ * 10 norm_bwd_static, 11 rms_final_reduce, 12 topk_fwd, 13 topk_bwd, 14 colsum_allreduce.
  * Returns -1 for an unknown code.
  */
 int qb_sizeof_args(int32_t which);

@@ -19,7 +19,7 @@ import torch
 QB_F32, QB_F16, QB_BF16 = 0, 1, 2
 QB_I32, QB_I64 = 0, 1
 QB_OK, QB_ERR_INVALID, QB_ERR_UNSUPPORTED, QB_ERR_CUDA = 0, -1, -2, -3
-QB_ABI_VERSION = 2
+QB_ABI_VERSION = 3
 
 FLOAT_CODES = {torch.float32: QB_F32, torch.float16: QB_F16, torch.bfloat16: QB_BF16}
 INDEX_CODES = {torch.int32: QB_I32, torch.int64: QB_I64}
@@ -98,6 +98,20 @@ class ColsumArgs(Structure):
     ]
 
 
+QB_MAX_PEERS = 8
+QB_PEER_HANDLE_BYTES = 64
+
+
+class ColsumAllreduceArgs(Structure):
+    _fields_ = [
+        ("partial0", c_void_p), ("partial1", c_void_p), ("out0", c_void_p), ("out1", c_void_p),
+        ("out0_f32", c_void_p), ("out1_f32", c_void_p), ("peers", c_void_p * QB_MAX_PEERS),
+        ("status", c_void_p), ("P", c_int64), ("cols", c_int64), ("cap_cols", c_int64),
+        ("num_buffers", c_int32), ("out_dtype", c_int32), ("world", c_int32), ("rank", c_int32),
+        ("seq", ctypes.c_uint32), ("pad0", c_int32),
+    ]
+
+
 class SoftmaxFwdArgs(Structure):
     _fields_ = [
         ("x", c_void_p), ("out", c_void_p), ("M", c_int64), ("N", c_int64),
@@ -168,6 +182,7 @@ _SIZEOF_CODES = {
     0: LaunchCfg, 1: NormFwdArgs, 2: NormBwdArgs, 3: ColsumArgs, 4: SoftmaxFwdArgs,
     5: SoftmaxBwdArgs, 6: CeFwdArgs, 7: CeBwdArgs, 8: CeCombineArgs, 9: DeviceInfo,
     10: NormBwdStaticArgs, 11: RmsFinalReduceArgs, 12: TopkFwdArgs, 13: TopkBwdArgs,
+    14: ColsumAllreduceArgs,
 }
 
 # every symbol include/quack_b200.h declares
@@ -176,6 +191,8 @@ EXPORTED_SYMBOLS = (
     "qb_softmax_bwd", "qb_ce_fwd", "qb_ce_bwd", "qb_ce_combine", "qb_query_device",
     "qb_last_error", "qb_abi_version", "qb_sizeof_args", "qb_norm_bwd_static",
     "qb_rms_final_reduce", "qb_ring_timeouts", "qb_last_kernel", "qb_topk_fwd", "qb_topk_bwd",
+    "qb_colsum_allreduce", "qb_peer_buffer_bytes", "qb_peer_buffer_create", "qb_peer_buffer_open",
+    "qb_peer_buffer_close", "qb_peer_buffer_destroy",
 )
 
 _LIB: Optional[ctypes.CDLL] = None
@@ -224,6 +241,7 @@ def lib() -> ctypes.CDLL:
         ("qb_ce_fwd", CeFwdArgs), ("qb_ce_bwd", CeBwdArgs), ("qb_ce_combine", CeCombineArgs),
         ("qb_norm_bwd_static", NormBwdStaticArgs), ("qb_rms_final_reduce", RmsFinalReduceArgs),
         ("qb_topk_fwd", TopkFwdArgs), ("qb_topk_bwd", TopkBwdArgs),
+        ("qb_colsum_allreduce", ColsumAllreduceArgs),
     ):
         fn = getattr(cdll, name)
         fn.restype = ctypes.c_int
@@ -234,6 +252,16 @@ def lib() -> ctypes.CDLL:
     cdll.qb_query_device.argtypes = [c_int32, POINTER(DeviceInfo)]
     cdll.qb_last_kernel.restype = c_char_p
     cdll.qb_last_kernel.argtypes = []
+    cdll.qb_peer_buffer_bytes.restype = c_int64
+    cdll.qb_peer_buffer_bytes.argtypes = [c_int32, c_int64]
+    cdll.qb_peer_buffer_create.restype = ctypes.c_int
+    cdll.qb_peer_buffer_create.argtypes = [c_int32, c_int64, POINTER(c_void_p), ctypes.c_char_p]
+    cdll.qb_peer_buffer_open.restype = ctypes.c_int
+    cdll.qb_peer_buffer_open.argtypes = [ctypes.c_char_p, POINTER(c_void_p)]
+    cdll.qb_peer_buffer_close.restype = ctypes.c_int
+    cdll.qb_peer_buffer_close.argtypes = [c_void_p]
+    cdll.qb_peer_buffer_destroy.restype = ctypes.c_int
+    cdll.qb_peer_buffer_destroy.argtypes = [c_void_p]
     cdll.qb_ring_timeouts.restype = ctypes.c_int
     cdll.qb_ring_timeouts.argtypes = [POINTER(ctypes.c_uint32)]
     _LIB = cdll

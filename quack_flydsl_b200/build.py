@@ -24,7 +24,7 @@ LIB_DIR = PKG_DIR / "lib"
 LIB_NAME = "libquack_b200.so"
 
 SOURCES = ["api.cu", "norm_fwd.cu", "norm_fwd_stream.cu", "norm_bwd.cu", "norm_bwd_ring.cu", "norm_bwd_static.cu",
-           "softmax.cu", "softmax_ring.cu", "cross_entropy.cu", "rms_final_reduce.cu", "topk.cu"]
+           "softmax.cu", "softmax_ring.cu", "softmax_cluster.cu", "cross_entropy.cu", "rms_final_reduce.cu", "topk.cu", "peer_reduce.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC"]
 

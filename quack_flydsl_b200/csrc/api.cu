@@ -264,6 +264,7 @@ extern "C" int qb_sizeof_args(int32_t which) {
     case 11: return (int)sizeof(qb_rms_final_reduce_args);
     case 12: return (int)sizeof(qb_topk_fwd_args);
     case 13: return (int)sizeof(qb_topk_bwd_args);
+    case 14: return (int)sizeof(qb_colsum_allreduce_args);
     default: return -1;
   }
 }

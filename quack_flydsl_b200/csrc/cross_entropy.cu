@@ -6,6 +6,11 @@
 // it), so any row length runs in one CTA; a cluster splits long rows only when there are too few
 // rows to fill the GPU.  Backward follows quack/cross_entropy.py:463-546
 // (CrossEntropyBackward.kernel): a purely elementwise 2-D grid.
+// Loads in this file use the default L2 policy instead of the evict-first "streaming" one:
+// measured on B200, evict-first loads lose 1-3 % here whenever L2 still holds lines that other
+// kernels left with the default policy (they are never displaced by evict-first traffic), while
+// default-policy loads run at the same speed in either state.  Stores stay evict-first.
+#define QB_LDG_MOD ""
 #include <type_traits>
 
 #include "common.cuh"

@@ -16,8 +16,8 @@
 // Every wait is bounded: a wait that has not succeeded after kRingTimeoutNs sets the CTA's abort
 // flag and bumps a device-side counter the host can read; from then on every wait of the CTA
 // returns at once, so a kernel that lost a signal runs to its end (with wrong results for the
-// affected rows) instead of hanging.  Copies only read this GPU's global memory and carry no
-// cluster-multicast qualifier.
+// affected rows) instead of hanging.  Copies only read this GPU's global memory, and each copy
+// has exactly one destination: the shared memory of the CTA that issued it.
 #pragma once
 
 #include "common.cuh"

@@ -5,6 +5,11 @@
 // (SoftmaxBackward.kernel).  A row is read once, kept in registers, and written once; rows longer
 // than one CTA's register capacity are split over a thread-block cluster whose CTAs exchange
 // their partials through distributed shared memory.
+// Loads in this file use the default L2 policy instead of the evict-first "streaming" one:
+// measured on B200, evict-first loads lose 1-3 % here whenever L2 still holds lines that other
+// kernels left with the default policy (they are never displaced by evict-first traffic), while
+// default-policy loads run at the same speed in either state.  Stores stay evict-first.
+#define QB_LDG_MOD ""
 #include <type_traits>
 
 #include "common.cuh"
@@ -215,7 +220,9 @@ __global__ void __launch_bounds__(T, (T >= 1024) ? 1 : (1024 / T)) softmax_strea
 
     float m = neg_inf(), s = 0.0f;  // forward: running max and sum 2^(x*log2e + off.hi)
     ExpOffset off = exp_offset(m);
-    float dot = 0.0f;               // backward: sum(dy * y)
+    float sv[BWD ? VEC : 1];        // backward: partial sums of dy * y
+#pragma unroll
+    for (int i = 0; i < (BWD ? VEC : 1); ++i) sv[i] = 0.0f;
 
     // ---- pass 1 ----
     auto pass1 = [&](auto full_tag, const char* q0, const char* q1, int c0) {
@@ -232,8 +239,7 @@ __global__ void __launch_bounds__(T, (T >= 1024) ? 1 : (1024 / T)) softmax_strea
           float v[VEC], y[VEC];
           unpack_chunk<DT, VEC>(v, r0[u], DT);
           unpack_chunk<DT, VEC>(y, r1[u], DT);  // padding chunks are zeros: they add nothing
-#pragma unroll
-          for (int i = 0; i < VEC; ++i) dot = fmaf(v[i], y[i], dot);
+          if constexpr (BWD) vfma<VEC>(sv, v, y, sv);
         }
       } else {
         // maximum of the whole block first, one re-basing of the partial sum per block
@@ -255,6 +261,8 @@ __global__ void __launch_bounds__(T, (T >= 1024) ? 1 : (1024 / T)) softmax_strea
           m = cm;
           off = nw;
         }
+        // (One scalar accumulator: packed partial sums need eight more registers, which this
+        // kernel, held to 64 by its 1024-thread CTAs, does not have -- measured 3 % slower.)
 #pragma unroll
         for (int u = 0; u < U; ++u) {
           if (FULL || c0 + u * T < nchunks) {
@@ -274,9 +282,9 @@ __global__ void __launch_bounds__(T, (T >= 1024) ? 1 : (1024 / T)) softmax_strea
       if (tail) pass1(std::false_type{}, q0, q1, tail_c0);
     }
 
-    float scale = 0.0f;
+    float scale = 0.0f, dot = 0.0f;
     if constexpr (BWD) {
-      dot = row_reduce<SumOp>(make_float2(dot, 0.f), g, scratch, 0, parity).x;
+      dot = row_reduce<SumOp>(make_float2(hsum<(BWD ? VEC : 1)>(sv), 0.f), g, scratch, 0, parity).x;
     } else {
       s *= fast_exp2(off.lo);
       const float2 ms = row_reduce<MaxSumExpOp>(make_float2(m, s), g, scratch, 0, parity);
@@ -306,6 +314,8 @@ __global__ void __launch_bounds__(T, (T >= 1024) ? 1 : (1024 / T)) softmax_strea
 #pragma unroll
           for (int i = 0; i < VEC; ++i) o[i] = y[i] * (v[i] - dot);
         } else {
+          // (Folding the normaliser into the exponent and packed fp32x2 arithmetic were tried
+          // here: 2 % slower at N = 65536 / 131072, the kernel sits at its 64-register limit.)
 #pragma unroll
           for (int i = 0; i < VEC; ++i) o[i] = fast_exp2(fmaf(v[i], kLog2e, off.hi)) * scale;
         }
@@ -460,12 +470,23 @@ static int softmax_dispatch(SoftmaxParams& p, bool uniform, int vec, const qb_la
     const int rc = plan_rows(opname, p.N, vec, caps, pref, k_target, 128, qb_launch_cfg{}, &probe);
     if (rc != QB_OK || probe.cluster_n > 1) {
       clear_error();
-      // Long rows.  Backward: staged once in a shared-memory ring by bulk copies (measured on
-      // B200, bf16: +2 % at N = 65536, +4 % at 131072, +12 % at 40960, +17 % at 262144 over
-      // re-reading the row from L2).  Forward: the L2 kernel; the ring version is within 1 % of
-      // it from N = 65536 and slower below (both are bound by the special function unit: two ex2
-      // per element), so it only runs when asked for.  What the ring cannot hold falls through.
-      const bool want_ring = BWD ? !(cfg.flags & QB_FLAG_NO_RING) : (cfg.flags & QB_FLAG_RING_FWD) != 0;
+      // Long rows.  Backward: the row is split over a thread-block cluster whose CTAs keep their
+      // slices in registers and exchange the row's dot product through distributed shared memory
+      // (softmax_cluster.cu; faster than the alternatives at every row length measured, see
+      // there); rows beyond its capacity fall through to the shared-memory ring and then to the
+      // two-pass L2 kernel.  Forward: the two-pass L2 kernel (bf16, 2 GiB per tensor, N = 65536 /
+      // 131072: 5.86 / 5.70 TB/s against 5.42 / 5.21 for the cluster kernel and 5.63 / 5.63 for
+      // the ring: the forward pass is bound by instruction issue and the special function unit,
+      // and the L2 kernel pays its per-row latency once per 128 KB instead of once per 32 KB).
+      // Flags pick one kernel explicitly.
+      const bool only_stream = (cfg.flags & QB_FLAG_NO_RING) != 0;
+      const bool want_cluster = !only_stream && ((cfg.flags & QB_FLAG_CLUSTER_REGS) || (BWD && !(cfg.flags & QB_FLAG_RING)));
+      const bool want_ring = !only_stream && (BWD || (cfg.flags & QB_FLAG_RING));
+      if (want_cluster) {
+        const int rc2 = launch_softmax_cluster<BWD>(p, cfg, dev, st);
+        if (rc2 != QB_ERR_UNSUPPORTED) return rc2;
+        clear_error();
+      }
       if (want_ring) {
         const int rr = launch_softmax_ring<BWD>(p, cfg, dev, st);
         if (rr != QB_ERR_UNSUPPORTED) return rr;

@@ -27,6 +27,12 @@ template <bool BWD>
 int launch_softmax_ring(const SoftmaxParams& p, const qb_launch_cfg& cfg, const DeviceFacts* dev,
                         cudaStream_t st);
 
+// Long rows split over a thread-block cluster with the slices held in registers and the next
+// rows' loads in flight (softmax_cluster.cu).  Same return convention as launch_softmax_ring.
+template <bool BWD>
+int launch_softmax_cluster(const SoftmaxParams& p, const qb_launch_cfg& cfg, const DeviceFacts* dev,
+                           cudaStream_t st);
+
 }  // namespace qb
 
 #endif  // QB_SOFTMAX_H_

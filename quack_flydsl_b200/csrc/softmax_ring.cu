@@ -50,7 +50,7 @@ __global__ void __launch_bounds__(T + 32, 1) softmax_ring_kernel(const SoftmaxRi
     // ---------------- producer warp (lane 0 issues) ----------------
     RingPos pos{0, 0u};
     int lap = 0;
-    const uint64_t pol = l2_policy(1);  // evict first: every byte is read once
+    const uint64_t pol = l2_policy((p.flags & 4) ? 2 : ((p.flags & 8) ? 0 : 1));
     for (int64_t row = cid; row < p.M; row += nclusters) {
       const char* s0 = reinterpret_cast<const char*>(p.in0) + (row * p.ld0 + col0) * ESZ;
       const char* s1 = BWD ? reinterpret_cast<const char*>(p.in1) + (row * p.ld1 + col0) * ESZ : nullptr;

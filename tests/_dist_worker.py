@@ -41,6 +41,33 @@ def main():
     dist.all_gather(gathered, dw)
     ok &= all(torch.equal(gathered[0], t) for t in gathered)
 
+    # The fused column-sum + peer all-reduce kernel against the same sum through NCCL: LayerNorm
+    # partials (two buffers), several steps in a row so that both parities and the step counter
+    # are exercised; every rank must obtain the same bits.
+    import importlib
+    rn = importlib.import_module("quack_flydsl_b200.rmsnorm")
+    par = sharded.PeerAllReduce(dev, cap_cols=2 * N)
+    gp = torch.Generator(device=dev).manual_seed(100 + rank)
+    for step in range(5):
+        P = 37 + step
+        dwp = torch.randn(P, N, device=dev, generator=gp)
+        dbp = torch.randn(P, N, device=dev, generator=gp)
+        o32 = torch.empty(2, N, device=dev)
+        o16 = torch.empty(2, N, device=dev, dtype=torch.bfloat16)
+        par.reduce([dwp, dbp], outs=[o16[0], o16[1]], outs_f32=[o32[0], o32[1]])
+        ref = torch.empty(2, N, device=dev)
+        rn._norm_bwd_colsum(dwp, ref[0])
+        rn._norm_bwd_colsum(dbp, ref[1])
+        parts = [torch.empty_like(ref) for _ in range(world)]
+        dist.all_gather(parts, ref)
+        tot = parts[0].clone()
+        for t in parts[1:]:
+            tot += t  # rank order, like the kernel
+        ok &= torch.equal(o32, tot)
+        ok &= torch.equal(o16, tot.bfloat16())
+    ok &= par.timeouts() == 0
+    par.close()
+
     Mc, Nc = 256, 128256
     logits = (2 * torch.randn(Mc, Nc, generator=g)).bfloat16()
     target = torch.randint(0, Nc, (Mc,), generator=g)

@@ -121,6 +121,31 @@ def test_row_sharded_norm_bwd_single_rank_matches_unsharded():
 
 
 @pytest.mark.gpu
+def test_peer_allreduce_single_rank_equals_column_sum():
+    """With one rank the fused column-sum + all-reduce kernel must reproduce qb_colsum bit for bit
+    (same summation order over P), for one and for two partial buffers, over several steps."""
+    rn = importlib.import_module("quack_flydsl_b200.rmsnorm")
+    dev = torch.device("cuda", 0)
+    par = sharded.PeerAllReduce(dev, cap_cols=8192)
+    try:
+        for step, (P, N, n) in enumerate([(296, 4096, 2), (148, 8192, 1), (5, 1000, 2), (1, 32, 1), (296, 4096, 2)]):
+            parts = [torch.randn(P, N, device=dev) for _ in range(n)]
+            o32 = [torch.empty(N, device=dev) for _ in range(n)]
+            o16 = [torch.empty(N, device=dev, dtype=torch.bfloat16) for _ in range(n)]
+            par.reduce(parts, outs=o16, outs_f32=o32)
+            for i in range(n):
+                ref = torch.empty(N, device=dev)
+                rn._norm_bwd_colsum(parts[i], ref)
+                assert torch.equal(o32[i], ref), (step, i)
+                assert torch.equal(o16[i], ref.bfloat16()), (step, i)
+        with pytest.raises(ValueError, match="exceed the exchange buffer"):
+            par.reduce([torch.randn(4, 8192, device=dev), torch.randn(4, 8192, device=dev)])
+        assert par.timeouts() == 0
+    finally:
+        par.close()
+
+
+@pytest.mark.gpu
 def test_multi_gpu_nccl_paths():
     """Launches tests/_dist_worker.py under torchrun on 2 GPUs, as the reference does for its own
     distributed tests (tests/test_distributed_gemm.py:363-389)."""
