@@ -1013,19 +1013,21 @@ def run_ours(args) -> None:
             else:
                 traffic_note = (f"profile summary is about {facts['kernel']}, the step ran {fwd_kernel}: "
                                 f"traffic not reported")
+        # `config` is the same object in both arms (ours and --impl reference); what is specific to
+        # this arm's step goes into `step_detail`.
         cfg = config_dict()
-        cfg.update({"step": "rmsnorm_fwd kernel + rmsnorm_bwd kernel + dw column-sum kernel"
-                            + (" + NCCL all-reduce of fp32 dw on a side stream, overlapping the next "
-                               "step's forward" if (world > 1 and not use_peer) else ""),
-                    "num_partials": P})
+        detail = {"kernels": "rmsnorm_fwd kernel + rmsnorm_bwd kernel + dw column-sum kernel", "num_partials": P}
         if use_peer:
-            cfg["step"] = ("rmsnorm_fwd kernel + rmsnorm_bwd kernel + one kernel that sums dw over the partial "
-                           "slices and over the GPUs (plain stores into peer-mapped buffers, flags, bounded waits) "
-                           "on a side stream, overlapping the next step's forward")
-            cfg["collective"] = "peer stores (qb_colsum_allreduce)"
-            cfg["collective_timeouts"] = peer.timeouts()
+            detail["kernels"] = ("rmsnorm_fwd kernel + rmsnorm_bwd kernel + one kernel that sums dw over the partial "
+                                 "slices and over the GPUs (plain stores into peer-mapped buffers, flags, bounded "
+                                 "waits) on a side stream, overlapping the next step's forward")
+            detail["collective"] = "peer stores (qb_colsum_allreduce)"
+            detail["collective_timeouts"] = peer.timeouts()
+        elif world > 1 and args.collective == "nccl":
+            detail["kernels"] += (" + NCCL all-reduce of fp32 dw on a side stream, overlapping the next step's forward")
+            detail["collective"] = "NCCL all-reduce"
         elif world > 1:
-            cfg["collective"] = "NCCL all-reduce"
+            detail["collective"] = "none (diagnostic run)"
         mhz = clocks.get("sm_mhz") if clocks else None
         line = {
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -1033,6 +1035,7 @@ def run_ours(args) -> None:
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "pct_of_8TBs": round(100 * value / (world * NOMINAL_HBM_GBS), 2),
             "config": cfg,
+            "step_detail": detail,
             "timing": {"blocks": len(blocks), "block_ms_median": round(ms_block, 4),
                        "block_ms_min": round(min(blocks), 4), "block_ms_max": round(max(blocks), 4),
                        "rule": f"blocks of {args.steps} steps repeated for >= {MIN_TIMED_SECONDS} s; median block",

@@ -630,6 +630,74 @@ __device__ __forceinline__ int64_t load_index(const void* base, int64_t idx, int
 // ---------------------------------------------------------------------------------------------
 // thread-block cluster primitives (PTX; valid only in kernels launched with a cluster dimension)
 // ---------------------------------------------------------------------------------------------
+// mbarrier / st.async primitives (shared by the cluster reductions below and the bulk-copy ring)
+// ---------------------------------------------------------------------------------------------
+constexpr unsigned long long kRingTimeoutNs = 2000000000ull;  // 2 s per wait
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ unsigned long long global_timer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ---- mbarrier primitives (shared::cta unless stated) ----
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ uint32_t mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok;
+}
+// Wait with cluster-scope acquire: pairs with mbar_arrive_remote of another CTA of the cluster.
+__device__ __forceinline__ uint32_t mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok;
+}
+// Address of the local shared-memory location `local` in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t map_to_cta(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+// st.async of 8 bytes into a peer CTA's shared memory; the bytes are counted on an mbarrier of that
+// peer (the reference's store_shared_remote + mbarrier pair, quack/utils.py:27-58).
+__device__ __forceinline__ void st_async_f2(uint32_t addr_cluster, float2 v, uint32_t bar_cluster) {
+  asm volatile(
+      "st.async.weak.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(
+          addr_cluster),
+      "f"(v.x), "f"(v.y), "r"(bar_cluster)
+      : "memory");
+}
+// Announces `bytes` on a local mbarrier and arrives on it, without a release fence (nothing this
+// thread wrote has to be published by the arrival; the data comes with the st.async stores).
+__device__ __forceinline__ void mbar_arrive_expect_tx_relaxed(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.relaxed.cta.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+// ---------------------------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t cluster_cta_rank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -693,7 +761,14 @@ constexpr int kRedStages = 2;       // independent reductions per row tile
 struct __align__(16) ReduceScratch {
   float2 warp_part[kRedStages][2][kMaxWarps];
   float2 cta_part[kRedStages][2][kClusterSlots];
+  unsigned long long bar[kRedStages][2];  // cluster exchange: counts the bytes of the partials
+  int abort;                              // set once a wait of this CTA timed out
+  // Kernels place their dynamic shared memory (staging rings, parameter slices) behind this
+  // struct; its size is kept a multiple of 1 KB so that those buffers start on the same
+  // boundary as before the barriers were added.
+  char pad[1024 - kRedStages * 2 * 8 - 16];
 };
+static_assert(sizeof(ReduceScratch) % 1024 == 0, "keeps dynamic shared memory 1 KB aligned");
 
 // Position of a thread in the row-tile geometry of its CTA.
 struct RowGeom {
@@ -721,6 +796,45 @@ __device__ __forceinline__ RowGeom make_geom(int tpr, int cluster_n) {
   g.cluster_n = cluster_n;
   g.crank = cluster_n > 1 ? cluster_cta_rank() : 0u;
   return g;
+}
+
+// Sets up the cluster exchange of row_reduce.  Every thread of the CTA calls it once, before the
+// kernel's barrier.cluster arrive / wait pair that precedes the first exchange (that pair
+// publishes the initialised barriers to the other CTAs of the cluster).
+__device__ __forceinline__ void reduce_init(ReduceScratch& s, int cluster_n) {
+  if (cluster_n > 1) {
+    if (threadIdx.x == 0) {
+#pragma unroll
+      for (int st = 0; st < kRedStages; ++st) {
+        mbar_init(smem_u32(&s.bar[st][0]), 1);
+        mbar_init(smem_u32(&s.bar[st][1]), 1);
+      }
+      s.abort = 0;
+      mbar_fence_init();
+    }
+    __syncthreads();
+  }
+}
+
+// Bounded wait on a local mbarrier: gives up after about a second (kReduceWaitCycles of the SM
+// clock, a 32-bit counter: one register), sets the CTA's abort flag (every later wait of the CTA
+// then returns at once) and bumps the device counter the host can read, so a lost signal costs
+// wrong results for the rows concerned, never a hung GPU.
+constexpr unsigned int kReduceWaitCycles = 0x70000000u;
+__device__ __forceinline__ void reduce_wait(ReduceScratch& s, uint32_t bar, uint32_t parity,
+                                            unsigned int* timeouts) {
+  if (mbar_try_wait(bar, parity) != 0) return;
+  const unsigned int t0 = static_cast<unsigned int>(clock());
+#pragma unroll 1
+  for (;;) {
+    if (mbar_try_wait(bar, parity) != 0) return;
+    if (*reinterpret_cast<volatile int*>(&s.abort)) return;
+    if (static_cast<unsigned int>(clock()) - t0 > kReduceWaitCycles) {
+      *reinterpret_cast<volatile int*>(&s.abort) = 1;
+      if (timeouts != nullptr) atomicAdd(timeouts, 1u);
+      return;
+    }
+  }
 }
 
 __device__ __forceinline__ float2 shfl_xor_f2(float2 v, int mask) {
@@ -751,9 +865,16 @@ __device__ __forceinline__ void row_group_sync(const RowGeom& g) {
   __syncthreads();
 }
 
-template <class Op, bool ROWBAR = false>
+// `rit` counts the rows this CTA has reduced so far: buffers (and, for clusters, barriers) are
+// double-buffered by its parity, and a barrier's phase is bit 1 of it.
+// CL = false compiles the cluster paths out (for kernels instantiated separately for
+// single-CTA rows: the exchange code costs registers that the norm backward does not have).
+// ASYNC = false keeps the cluster exchange on plain remote stores published by barrier.cluster
+// (fewer registers; see the note in the function).
+template <class Op, bool ROWBAR = false, bool CL = true, bool ASYNC = true>
 __device__ __forceinline__ float2 row_reduce(float2 v, const RowGeom& g, ReduceScratch& s,
-                                             int stage, int parity) {
+                                             int stage, int rit, unsigned int* timeouts = nullptr) {
+  const int parity = rit & 1;
   // 1. within the warp (or the sub-warp row group)
   if (g.tpr >= 32) {
 #pragma unroll
@@ -761,17 +882,37 @@ __device__ __forceinline__ float2 row_reduce(float2 v, const RowGeom& g, ReduceS
   } else {
     for (int o = g.tpr >> 1; o > 0; o >>= 1) v = Op::combine(v, shfl_xor_f2(v, o));
   }
-  if (g.cluster_n > 1) {
+  if (CL && g.cluster_n > 1) {
     // 2+3 (cluster): every warp pushes its partial into slot [crank * warps + warp] of every
-    //    CTA's buffer through distributed shared memory, ONE cluster barrier publishes the
-    //    stores (it also orders the warps of this CTA), and every warp folds all slots in the
-    //    same order, so all CTAs obtain bit-identical results.
+    //    CTA's buffer through distributed shared memory, every thread waits until all partials
+    //    have arrived in its own CTA's buffer, and every warp folds all slots in the same order,
+    //    so all CTAs obtain bit-identical results.
     const int nslots = g.warps_per_row * g.cluster_n;
     if (nslots <= kClusterSlots) {
+      // The partials travel by st.async and are counted on an mbarrier of the receiving CTA
+      // instead of being published by barrier.cluster: that barrier's arrive has release
+      // semantics, which stalls the thread until its global loads and stores in flight have
+      // completed -- in a persistent kernel the previous row's stores and the next row's
+      // prefetch (measured on the softmax backward: 5.6 -> 6.8 TB/s at N = 65536).  Buffer and
+      // barrier [stage][parity] are reused every second row; a peer can only send row j + 2
+      // after every warp of this CTA has sent row j + 1, hence after it has folded row j.
       float2* buf = s.cta_part[stage][parity];
-      if (g.lane < g.cluster_n)
-        st_shared_cluster_f2(&buf[g.crank * g.warps_per_row + g.warp_in_row], g.lane, v);
-      cluster_sync_all();
+      if constexpr (ASYNC) {
+        const uint32_t phase = static_cast<uint32_t>(rit >> 1) & 1u;
+        const uint32_t bar = smem_u32(&s.bar[stage][parity]);
+        if (threadIdx.x == 0) mbar_arrive_expect_tx_relaxed(bar, static_cast<uint32_t>(nslots) * 8u);
+        if (g.lane < g.cluster_n)
+          st_async_f2(map_to_cta(smem_u32(&buf[g.crank * g.warps_per_row + g.warp_in_row]), g.lane), v,
+                      map_to_cta(bar, g.lane));
+        reduce_wait(s, bar, phase, timeouts);
+      } else {
+        // The exchange above costs about six registers more than this one.  The LayerNorm
+        // backward with db accumulators and run-time geometry has none to spare (it spilled and
+        // lost 20 %), so it stays on plain remote stores + one barrier.cluster round trip.
+        if (g.lane < g.cluster_n)
+          st_shared_cluster_f2(&buf[g.crank * g.warps_per_row + g.warp_in_row], g.lane, v);
+        cluster_sync_all();
+      }
       float2 acc = Op::identity();
       for (int i = g.lane; i < nslots; i += 32) acc = Op::combine(acc, buf[i]);
 #pragma unroll
@@ -791,7 +932,7 @@ __device__ __forceinline__ float2 row_reduce(float2 v, const RowGeom& g, ReduceS
   // 3. across the CTAs of the cluster (only when the one-step exchange above does not fit):
   //    every CTA pushes its partial into slot [crank] of every CTA's buffer, a cluster barrier
   //    publishes the stores, and all CTAs fold the slots in rank order.
-  if (g.cluster_n > 1) {
+  if (CL && g.cluster_n > 1) {
     float2* buf = s.cta_part[stage][parity];
     if (threadIdx.x < g.cluster_n) st_shared_cluster_f2(&buf[g.crank], threadIdx.x, v);
     cluster_sync_all();

@@ -23,6 +23,7 @@ struct CeFwdParams {
   int tpr, rows_per_cta, cluster_n, cols_per_cta;
   int64_t num_tiles;
   int flags;  // qb_launch_cfg.flags
+  unsigned int* timeouts;  // device counter of cluster-exchange waits that gave up
 };
 
 // A target names a class only if it is not ignore_index and lies inside [0, num_classes) (no upper
@@ -38,6 +39,7 @@ __global__ void __launch_bounds__(512) ce_fwd_kernel(const CeFwdParams p) {
   __shared__ ReduceScratch scratch;
   const qb_ce_fwd_args& a = p.a;
   const RowGeom g = make_geom(p.tpr, p.cluster_n);
+  reduce_init(scratch, p.cluster_n);
   if (p.cluster_n > 1) cluster_arrive();
   const int N = static_cast<int>(a.N);
   const int col0 = static_cast<int>(g.crank) * p.cols_per_cta;
@@ -45,7 +47,7 @@ __global__ void __launch_bounds__(512) ce_fwd_kernel(const CeFwdParams p) {
   const int nchunks = ncols > 0 ? ncols / VEC : 0;
 
   const int64_t tile_stride = gridDim.x / p.cluster_n;
-  int parity = 0;
+  int rit = 0;
   bool first = true;
   for (int64_t tile = blockIdx.x / p.cluster_n; tile < p.num_tiles; tile += tile_stride) {
     const int64_t row = tile * p.rows_per_cta + g.r;
@@ -89,8 +91,8 @@ __global__ void __launch_bounds__(512) ce_fwd_kernel(const CeFwdParams p) {
 
     if (first && p.cluster_n > 1) cluster_wait();
     first = false;
-    const float2 ms = row_reduce<MaxSumExpOp>(make_float2(m, s), g, scratch, 0, parity);
-    parity ^= 1;
+    const float2 ms = row_reduce<MaxSumExpOp>(make_float2(m, s), g, scratch, 0, rit, p.timeouts);
+    ++rit;
 
     if (row_ok && g.t == 0 && g.crank == 0) {
       const int64_t tgt = load_index(a.target, row, a.target_dtype);
@@ -151,7 +153,7 @@ __global__ void __launch_bounds__(T, (T >= 1024) ? 1 : (1024 / T)) ce_fwd_dx_ker
   const int tail_c0 = nfull * (T * U) + g.t;
   const uint64_t keep = l2_policy((p.flags & 4) ? 2 : 0);
   const uint64_t drop = l2_policy((p.flags & 8) ? 2 : 1);
-  int parity = 0;
+  int rit = 0;
   for (int64_t row = blockIdx.x; row < a.M; row += gridDim.x) {
     const char* xin = reinterpret_cast<const char*>(a.x) + (row * a.x_row_stride * (16 / VEC) + g.t * 16);
     char* dxo = reinterpret_cast<char*>(a.dx) + (row * a.dx_row_stride * (16 / VEC) + g.t * 16);
@@ -219,8 +221,8 @@ __global__ void __launch_bounds__(T, (T >= 1024) ? 1 : (1024 / T)) ce_fwd_dx_ker
       if (tail) pass1(std::false_type{}, q, tail_c0);
     }
     s *= fast_exp2(off.lo);
-    const float2 ms = row_reduce<MaxSumExpOp>(make_float2(m, s), g, scratch, 0, parity);
-    parity ^= 1;
+    const float2 ms = row_reduce<MaxSumExpOp>(make_float2(m, s), g, scratch, 0, rit, p.timeouts);
+    ++rit;
     const float log_s = logf(ms.y);
     const float lse = ms.x + log_s;
     if (g.t == 0) {
@@ -523,6 +525,7 @@ extern "C" int qb_ce_fwd(const qb_ce_fwd_args* args, qb_stream_t stream) {
     if (vd.vec == 16 / host_dtype_bytes(a.x_dtype) && a.cfg.cluster_n == 0 &&
         !(a.cfg.flags & 2) && a.M >= dev->sm_count && row_bytes >= (64 << 10)) {
       CeFwdParams p;
+      p.timeouts = nullptr;
       p.a = a;
       p.tpr = 0;
       p.rows_per_cta = 1;
@@ -575,6 +578,11 @@ extern "C" int qb_ce_fwd(const qb_ce_fwd_args* args, qb_stream_t stream) {
   p.tpr = tpr;
   p.rows_per_cta = threads / tpr;
   p.cluster_n = cluster_n;
+  p.timeouts = nullptr;
+  if (cluster_n > 1) {
+    p.timeouts = ring_timeout_counter();
+    if (p.timeouts == nullptr) return QB_ERR_CUDA;
+  }
   p.cols_per_cta = static_cast<int>(ceil_div(chunks, cluster_n) * vec);
   p.num_tiles = ceil_div(a.M, p.rows_per_cta);
   p.flags = a.cfg.flags;

@@ -25,6 +25,7 @@ struct NormBwdParams {
   int64_t num_tiles;
   int stages;  // shared-memory ring depth (>= 1)
   int n_in;    // streamed inputs per row: 2 (x, dout) or 3 (+ dresidual_out)
+  unsigned int* timeouts;  // device counter of cluster-exchange waits that gave up
 };
 
 constexpr int kMaxStages = 8;
@@ -54,15 +55,21 @@ __device__ __forceinline__ void cp_async_wait_dyn(int n) {
 // chunk strides then become immediate offsets of the loads and stores.  This kernel is
 // instruction-issue-bound, and the run-time strides cost LayerNorm backward 6 % (measured, bf16
 // N = 4096).  TPR == 0 takes both from the launch.
-template <int DT, int VEC, int K, bool LN, bool DB, int TPR = 0>
+// CL: the row may be shared by the CTAs of a cluster (p.cluster_n > 1).  Single-CTA rows get an
+// instantiation of their own without the cluster exchange: this kernel sits at the 255-register
+// limit, and the exchange code pushed the LayerNorm + db variant into spills (N = 16384:
+// 5.3 -> 3.8 TB/s) when both lived in one kernel.
+template <int DT, int VEC, int K, bool LN, bool DB, int TPR = 0, bool CL = false>
 __global__ void __launch_bounds__((K * VEC <= 8) ? 1024 : ((K * VEC <= 16) ? 512 : 256))
 norm_bwd_kernel(const NormBwdParams p) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ ReduceScratch scratch;
   const qb_norm_bwd_args& a = p.a;
   const int ptpr = TPR ? TPR : p.tpr;
-  const RowGeom g = make_geom(ptpr, p.cluster_n);
-  if (p.cluster_n > 1) cluster_arrive();
+  const int cn = CL ? p.cluster_n : 1;
+  const RowGeom g = make_geom(ptpr, cn);
+  reduce_init(scratch, cn);
+  if (cn > 1) cluster_arrive();
 
   constexpr int kSlot = RawWords<DT, VEC>::value * 4;  // bytes of one staged chunk
   const int N = static_cast<int>(a.N);
@@ -112,8 +119,8 @@ norm_bwd_kernel(const NormBwdParams p) {
             step_dx = cstride * esz_dx, step_dr = cstride * esz_dr;
 
   // Shared-memory ring: stage s, input j, chunk k, thread tid -> one slot of kSlot bytes.
-  const int64_t P = gridDim.x / p.cluster_n;
-  const int64_t pidx = blockIdx.x / p.cluster_n;
+  const int64_t P = gridDim.x / cn;
+  const int64_t pidx = blockIdx.x / cn;
   const int chunk_bytes = nthreads * kSlot;           // between chunks k and k + 1
   const int in_bytes = K * chunk_bytes;               // one input of one stage
   const int stage_bytes = p.n_in * in_bytes;          // one stage
@@ -170,7 +177,7 @@ norm_bwd_kernel(const NormBwdParams p) {
     }
   }
 
-  int parity = 0;
+  int rit = 0;
   bool first = true;
   int it = 0;
   for (int64_t tile = pidx; tile < p.num_tiles; tile += P, ++it) {
@@ -222,10 +229,10 @@ norm_bwd_kernel(const NormBwdParams p) {
     if (mode != 0) pass1(std::integral_constant<int, 2>{}); else pass1(std::integral_constant<int, 0>{});
     const float s1 = hsum<VEC>(s1v);
     const float s2 = LN ? hsum<VEC>(s2v) : 0.0f;
-    if (first && p.cluster_n > 1) cluster_wait();
+    if (first && cn > 1) cluster_wait();
     first = false;
-    const float2 red = row_reduce<SumOp>(make_float2(s1, s2), g, scratch, 0, parity);
-    parity ^= 1;
+    const float2 red = row_reduce<SumOp, false, CL, !(LN && DB && TPR == 0)>(make_float2(s1, s2), g, scratch, 0, rit, p.timeouts);
+    ++rit;
     const float ca = rstd;
     const float cb = -rstd * rstd * rstd * red.x * inv_n;
     const float cc = LN ? -rstd * red.y * inv_n : 0.0f;
@@ -270,7 +277,7 @@ norm_bwd_kernel(const NormBwdParams p) {
     else if (mode == 1) pass2(std::integral_constant<int, 1>{});
     else pass2(std::integral_constant<int, 0>{});
   }
-  if (first && p.cluster_n > 1) cluster_wait();
+  if (first && cn > 1) cluster_wait();
   cp_async_wait<0>();
 
   // ---- epilogue: this CTA's partial sums -> row pidx of the [P, H, N] workspaces ----
@@ -358,27 +365,34 @@ __global__ void __launch_bounds__(256) colsum_kernel(const ColsumParams p) {
 // ---------------------------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------------------------
-template <int DT, int VEC, int K, int TPR>
-static int launch_norm_bwd_t(const NormBwdParams& p, dim3 grid, int threads, size_t smem,
+template <int DT, int VEC, int K, int TPR, bool CL>
+static int launch_norm_bwd_c(const NormBwdParams& p, dim3 grid, int threads, size_t smem,
                              cudaStream_t st) {
   const bool ln = p.a.is_layernorm != 0;
   const bool db = p.a.db_partial != nullptr;
   if constexpr (DT == kDynDT) {
     // The generic path always carries db accumulators (written only when requested).
-    if (ln) return launch_kernel(norm_bwd_kernel<DT, VEC, K, true, true, TPR>, grid, threads, smem,
+    if (ln) return launch_kernel(norm_bwd_kernel<DT, VEC, K, true, true, TPR, CL>, grid, threads, smem,
                                  p.cluster_n, st, p, "layernorm_bwd");
-    return launch_kernel(norm_bwd_kernel<DT, VEC, K, false, true, TPR>, grid, threads, smem,
+    return launch_kernel(norm_bwd_kernel<DT, VEC, K, false, true, TPR, CL>, grid, threads, smem,
                          p.cluster_n, st, p, "rmsnorm_bwd");
   } else {
-    if (ln && db) return launch_kernel(norm_bwd_kernel<DT, VEC, K, true, true, TPR>, grid, threads,
+    if (ln && db) return launch_kernel(norm_bwd_kernel<DT, VEC, K, true, true, TPR, CL>, grid, threads,
                                        smem, p.cluster_n, st, p, "layernorm_bwd");
-    if (ln) return launch_kernel(norm_bwd_kernel<DT, VEC, K, true, false, TPR>, grid, threads, smem,
+    if (ln) return launch_kernel(norm_bwd_kernel<DT, VEC, K, true, false, TPR, CL>, grid, threads, smem,
                                  p.cluster_n, st, p, "layernorm_bwd");
-    if (db) return launch_kernel(norm_bwd_kernel<DT, VEC, K, false, true, TPR>, grid, threads, smem,
+    if (db) return launch_kernel(norm_bwd_kernel<DT, VEC, K, false, true, TPR, CL>, grid, threads, smem,
                                  p.cluster_n, st, p, "rmsnorm_bwd");
-    return launch_kernel(norm_bwd_kernel<DT, VEC, K, false, false, TPR>, grid, threads, smem,
+    return launch_kernel(norm_bwd_kernel<DT, VEC, K, false, false, TPR, CL>, grid, threads, smem,
                          p.cluster_n, st, p, "rmsnorm_bwd");
   }
+}
+
+template <int DT, int VEC, int K, int TPR>
+static int launch_norm_bwd_t(const NormBwdParams& p, dim3 grid, int threads, size_t smem,
+                             cudaStream_t st) {
+  if (p.cluster_n > 1) return launch_norm_bwd_c<DT, VEC, K, TPR, true>(p, grid, threads, smem, st);
+  return launch_norm_bwd_c<DT, VEC, K, TPR, false>(p, grid, threads, smem, st);
 }
 
 template <int DT, int VEC, int K>
@@ -464,8 +478,8 @@ static int default_num_partials(const NormBwdPlan& plan, const DeviceFacts* dev)
     // second wave and nearly doubles the time, so ask the occupancy calculator.  All stage-1
     // instantiations have the same footprint class; the plainest one stands for them.
     const void* rep = plan.rows.vec == 4
-                          ? reinterpret_cast<const void*>(norm_bwd_kernel<QB_F32, 4, 8, false, false, 0>)
-                          : reinterpret_cast<const void*>(norm_bwd_kernel<QB_BF16, 8, 8, false, false, 0>);
+                          ? reinterpret_cast<const void*>(norm_bwd_kernel<QB_F32, 4, 8, false, false, 0, true>)
+                          : reinterpret_cast<const void*>(norm_bwd_kernel<QB_BF16, 8, 8, false, false, 0, true>);
     const int n = cached_max_clusters(rep, plan.rows.threads, plan.smem, plan.rows.cluster_n);
     if (n > 0 && n < clusters) clusters = n;
   }
@@ -567,6 +581,11 @@ extern "C" int qb_norm_bwd(const qb_norm_bwd_args* args, qb_stream_t stream) {
   p.tpr = plan.rows.tpr;
   p.rows_per_cta = plan.rows.rows_per_cta;
   p.cluster_n = plan.rows.cluster_n;
+  p.timeouts = nullptr;
+  if (p.cluster_n > 1) {
+    p.timeouts = ring_timeout_counter();
+    if (p.timeouts == nullptr) return QB_ERR_CUDA;
+  }
   p.cols_per_cta = plan.rows.cols_per_cta;
   p.num_tiles = ceil_div(a.M, p.rows_per_cta);
   p.stages = plan.stages;

@@ -31,6 +31,7 @@ norm_fwd_kernel(const NormFwdParams p) {
   __shared__ ReduceScratch scratch;
   const qb_norm_fwd_args& a = p.a;
   const RowGeom g = make_geom(p.tpr, p.cluster_n);
+  reduce_init(scratch, p.cluster_n);
   if (p.cluster_n > 1) cluster_arrive();  // completed by cluster_wait() before the first exchange
 
   const int N = static_cast<int>(a.N);
@@ -121,7 +122,7 @@ norm_fwd_kernel(const NormFwdParams p) {
   const int chunk0 = g.t;  // chunk k of this thread is slice chunk chunk0 + k * tpr
 
   const int64_t tile_stride = gridDim.x / p.cluster_n;
-  int parity = 0;
+  int rit = 0;
   bool first = true;
   for (int64_t tile = blockIdx.x / p.cluster_n; tile < p.num_tiles; tile += tile_stride) {
     const int64_t m = tile * p.rows_per_cta + g.r;
@@ -191,7 +192,7 @@ norm_fwd_kernel(const NormFwdParams p) {
           vadd<VEC>(sv, sv, v[k]);
         }
       }
-      mean = row_reduce<SumOp, true>(make_float2(hsum<VEC>(sv), 0.f), g, scratch, 0, parity).x * inv_n;
+      mean = row_reduce<SumOp, true>(make_float2(hsum<VEC>(sv), 0.f), g, scratch, 0, rit, p.timeouts).x * inv_n;
       // sum (x - mean)^2; padding chunks hold zeros and get offset 0 instead of -mean
       float qv[VEC];
 #pragma unroll
@@ -211,7 +212,7 @@ norm_fwd_kernel(const NormFwdParams p) {
         vfma<VEC>(qv, d, d, qv);
       }
       const float var =
-          row_reduce<SumOp, true>(make_float2(hsum<VEC>(qv), 0.f), g, scratch, 1, parity).x * inv_n;
+          row_reduce<SumOp, true>(make_float2(hsum<VEC>(qv), 0.f), g, scratch, 1, rit, p.timeouts).x * inv_n;
       rstd = rsqrtf(var + a.eps);
     } else {
       float qv[VEC];
@@ -228,10 +229,10 @@ norm_fwd_kernel(const NormFwdParams p) {
         }
       }
       const float ms =
-          row_reduce<SumOp, true>(make_float2(hsum<VEC>(qv), 0.f), g, scratch, 0, parity).x * inv_n;
+          row_reduce<SumOp, true>(make_float2(hsum<VEC>(qv), 0.f), g, scratch, 0, rit, p.timeouts).x * inv_n;
       rstd = rsqrtf(ms + a.eps);
     }
-    parity ^= 1;
+    ++rit;
 
     if (row_ok && g.t == 0 && g.crank == 0) {
       if (a.rstd != nullptr) a.rstd[row] = rstd;
@@ -412,6 +413,7 @@ extern "C" int qb_norm_fwd(const qb_norm_fwd_args* args, qb_stream_t stream) {
                    a.x_dtype != QB_F32 && !(a.cfg.flags & 1);
 
   NormFwdParams p;
+  p.timeouts = nullptr;
   p.a = a;
   p.flags = a.cfg.flags;
   // Long rows with at least one row per SM: the streamed two-pass kernel with the row parked in
@@ -480,6 +482,10 @@ extern "C" int qb_norm_fwd(const qb_norm_fwd_args* args, qb_stream_t stream) {
   p.tpr = plan.tpr;
   p.rows_per_cta = plan.rows_per_cta;
   p.cluster_n = plan.cluster_n;
+  if (p.cluster_n > 1) {
+    p.timeouts = ring_timeout_counter();
+    if (p.timeouts == nullptr) return QB_ERR_CUDA;
+  }
   p.cols_per_cta = plan.cols_per_cta;
   p.num_tiles = ceil_div(a.M, p.rows_per_cta);
   // fp32 (weight + offset) and bias slices of this CTA's columns (ones / zeros when absent), if

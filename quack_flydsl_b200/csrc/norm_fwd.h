@@ -16,6 +16,7 @@ struct NormFwdParams {
   int64_t num_tiles;  // ceil(M / rows_per_cta)
   int stage_params;   // weight / bias slices are staged in shared memory
   int flags;          // qb_launch_cfg.flags
+  unsigned int* timeouts;  // device counter of cluster-exchange waits that gave up
 };
 
 // Launches the streamed two-pass kernel for p (uniform dtype, one row per CTA of `threads`).

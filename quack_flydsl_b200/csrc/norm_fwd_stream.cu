@@ -39,7 +39,7 @@ __global__ void __launch_bounds__(T, 512 / T) norm_fwd_stream_kernel(const NormF
   const uint64_t keep = l2_policy((p.flags & 4) ? 2 : 0);
   const uint64_t drop = l2_policy((p.flags & 8) ? 2 : 1);
   const bool has_w = a.weight != nullptr, has_b = a.bias != nullptr;
-  int parity = 0;
+  int rit = 0;
   for (int64_t row = blockIdx.x; row < a.M; row += gridDim.x) {
     const char* xin = reinterpret_cast<const char*>(a.x) + (row * a.x_row_stride * (16 / VEC) + g.t * 16);
     const char* rin = RES ? reinterpret_cast<const char*>(a.residual) +
@@ -132,16 +132,16 @@ __global__ void __launch_bounds__(T, 512 / T) norm_fwd_stream_kernel(const NormF
     float rstd, mean = 0.0f;
     if constexpr (LN) {
       // mean = sum(cnt_t * mu_t) / N;  M2 = sum(m2_t + cnt_t * (mu_t - mean)^2)
-      const float2 r1 = row_reduce<SumOp>(make_float2(cnt * mu, 0.0f), g, scratch, 0, parity);
+      const float2 r1 = row_reduce<SumOp>(make_float2(cnt * mu, 0.0f), g, scratch, 0, rit);
       mean = r1.x * inv_n;
       const float dm = mu - mean;
-      const float2 r2 = row_reduce<SumOp>(make_float2(m2 + cnt * dm * dm, 0.0f), g, scratch, 1, parity);
+      const float2 r2 = row_reduce<SumOp>(make_float2(m2 + cnt * dm * dm, 0.0f), g, scratch, 1, rit);
       rstd = rsqrtf(r2.x * inv_n + a.eps);
     } else {
-      const float2 r1 = row_reduce<SumOp>(make_float2(ssq + ssq2, 0.0f), g, scratch, 0, parity);
+      const float2 r1 = row_reduce<SumOp>(make_float2(ssq + ssq2, 0.0f), g, scratch, 0, rit);
       rstd = rsqrtf(r1.x * inv_n + a.eps);
     }
-    parity ^= 1;
+    ++rit;
     if (g.t == 0) {
       if (a.rstd != nullptr) a.rstd[row] = rstd;
       if (LN && a.mean != nullptr) a.mean[row] = mean;

@@ -30,6 +30,7 @@ softmax_fwd_kernel(const SoftmaxParams p) {
   __shared__ ReduceScratch scratch;
   const int ptpr = TPR ? TPR : p.tpr;
   const RowGeom g = make_geom(ptpr, p.cluster_n);
+  reduce_init(scratch, p.cluster_n);
   if (p.cluster_n > 1) cluster_arrive();
   const int col0 = static_cast<int>(g.crank) * p.cols_per_cta;
   const int ncols = min(p.cols_per_cta, p.N - col0);
@@ -38,7 +39,7 @@ softmax_fwd_kernel(const SoftmaxParams p) {
   const int nchunks = ncols > 0 ? ncols / VEC : 0;
   const int nk = nchunks > g.t ? min(K, (nchunks - g.t + ptpr - 1) / ptpr) : 0;
   const int64_t tile_stride = gridDim.x / p.cluster_n;
-  int parity = 0;
+  int rit = 0;
   bool first = true;
   for (int64_t tile = blockIdx.x / p.cluster_n; tile < p.num_tiles; tile += tile_stride) {
     const int64_t row = tile * p.rows_per_cta + g.r;
@@ -96,8 +97,8 @@ softmax_fwd_kernel(const SoftmaxParams p) {
     s_t *= corr;
     if (first && p.cluster_n > 1) cluster_wait();
     first = false;
-    const float2 ms = row_reduce<MaxSumExpOp>(make_float2(m_t, s_t), g, scratch, 0, parity);
-    parity ^= 1;
+    const float2 ms = row_reduce<MaxSumExpOp>(make_float2(m_t, s_t), g, scratch, 0, rit, p.timeouts);
+    ++rit;
     // y_i = e_i * exp(m_t - m) / s
     const float scale = (m_t == neg_inf())
                             ? 0.0f
@@ -130,6 +131,7 @@ __global__ void __launch_bounds__((K * VEC > 16) ? 512 : 1024)
 softmax_bwd_kernel(const SoftmaxParams p) {
   __shared__ ReduceScratch scratch;
   const RowGeom g = make_geom(p.tpr, p.cluster_n);
+  reduce_init(scratch, p.cluster_n);
   if (p.cluster_n > 1) cluster_arrive();
   const int col0 = static_cast<int>(g.crank) * p.cols_per_cta;
   const int ncols = min(p.cols_per_cta, p.N - col0);
@@ -138,7 +140,7 @@ softmax_bwd_kernel(const SoftmaxParams p) {
   const int nchunks = ncols > 0 ? ncols / VEC : 0;
   const int nk = nchunks > g.t ? min(K, (nchunks - g.t + p.tpr - 1) / p.tpr) : 0;
   const int64_t tile_stride = gridDim.x / p.cluster_n;
-  int parity = 0;
+  int rit = 0;
   bool first = true;
   for (int64_t tile = blockIdx.x / p.cluster_n; tile < p.num_tiles; tile += tile_stride) {
     const int64_t row = tile * p.rows_per_cta + g.r;
@@ -166,8 +168,8 @@ softmax_bwd_kernel(const SoftmaxParams p) {
     }
     if (first && p.cluster_n > 1) cluster_wait();
     first = false;
-    dot = row_reduce<SumOp>(make_float2(dot, 0.f), g, scratch, 0, parity).x;
-    parity ^= 1;
+    dot = row_reduce<SumOp>(make_float2(dot, 0.f), g, scratch, 0, rit, p.timeouts).x;
+    ++rit;
 #pragma unroll
     for (int k = 0; k < K; ++k) {
       float dy[VEC], y[VEC], dx[VEC];
@@ -211,7 +213,7 @@ __global__ void __launch_bounds__(T, (T >= 1024) ? 1 : (1024 / T)) softmax_strea
   const int tail_c0 = nfull * (T * U) + g.t;     // this thread's first chunk of the partial block
   const uint64_t keep = l2_policy((p.flags & 4) ? 2 : 0);
   const uint64_t drop = l2_policy((p.flags & 8) ? 2 : 1);
-  int parity = 0;
+  int rit = 0;
   for (int64_t row = blockIdx.x; row < p.M; row += gridDim.x) {
     const char* in0 = reinterpret_cast<const char*>(p.in0) + (row * p.ld0 * (16 / VEC) + g.t * 16);
     const char* in1 = BWD ? reinterpret_cast<const char*>(p.in1) + (row * p.ld1 * (16 / VEC) + g.t * 16)
@@ -284,14 +286,14 @@ __global__ void __launch_bounds__(T, (T >= 1024) ? 1 : (1024 / T)) softmax_strea
 
     float scale = 0.0f, dot = 0.0f;
     if constexpr (BWD) {
-      dot = row_reduce<SumOp>(make_float2(hsum<(BWD ? VEC : 1)>(sv), 0.f), g, scratch, 0, parity).x;
+      dot = row_reduce<SumOp>(make_float2(hsum<(BWD ? VEC : 1)>(sv), 0.f), g, scratch, 0, rit, p.timeouts).x;
     } else {
       s *= fast_exp2(off.lo);
-      const float2 ms = row_reduce<MaxSumExpOp>(make_float2(m, s), g, scratch, 0, parity);
+      const float2 ms = row_reduce<MaxSumExpOp>(make_float2(m, s), g, scratch, 0, rit, p.timeouts);
       off = exp_offset(ms.x);
       scale = ms.x == neg_inf() ? 0.0f : fast_exp2(off.lo) * (1.0f / ms.y);
     }
-    parity ^= 1;
+    ++rit;
 
     // ---- pass 2: newest lines first ----
     auto pass2 = [&](auto full_tag, const char* q0, const char* q1, char* qo, int c0) {
@@ -499,6 +501,10 @@ static int softmax_dispatch(SoftmaxParams& p, bool uniform, int vec, const qb_la
   p.tpr = plan.tpr;
   p.rows_per_cta = plan.rows_per_cta;
   p.cluster_n = plan.cluster_n;
+  if (p.cluster_n > 1) {
+    p.timeouts = ring_timeout_counter();
+    if (p.timeouts == nullptr) return QB_ERR_CUDA;
+  }
   p.cols_per_cta = plan.cols_per_cta;
   p.num_tiles = ceil_div(p.M, p.rows_per_cta);
   // Rows owned by a single CTA: one tile per CTA (nothing to amortise, and the hardware block

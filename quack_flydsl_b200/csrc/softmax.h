@@ -18,6 +18,7 @@ struct SoftmaxParams {
   int tpr, rows_per_cta, cluster_n, cols_per_cta;
   int64_t num_tiles;
   int flags;  // qb_launch_cfg.flags
+  unsigned int* timeouts;  // device counter of cluster-exchange waits that gave up
 };
 
 // Long rows through the bulk-copy shared-memory ring (softmax_ring.cu).  Returns QB_OK after the

@@ -37,20 +37,6 @@ struct __align__(16) ClusterScratch {
   int abort;                        // set once a wait of this CTA timed out
 };
 
-// st.async of 8 bytes into a peer's shared memory; the bytes are counted on the peer's mbarrier.
-__device__ __forceinline__ void st_async_f2(uint32_t addr_cluster, float2 v, uint32_t bar_cluster) {
-  asm volatile(
-      "st.async.weak.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(
-          addr_cluster),
-      "f"(v.x), "f"(v.y), "r"(bar_cluster)
-      : "memory");
-}
-// Announces `bytes` on a local mbarrier and arrives on it, without a release fence (nothing this
-// thread wrote has to be published by the arrival; the data comes with the st.async stores).
-__device__ __forceinline__ void mbar_arrive_expect_tx_relaxed(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.relaxed.cta.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
-               : "memory");
-}
 // Bounded wait on a local mbarrier (see ring_wait).
 __device__ __forceinline__ void cluster_row_wait(ClusterScratch* sc, uint32_t bar, uint32_t parity,
                                                  unsigned int* timeouts) {

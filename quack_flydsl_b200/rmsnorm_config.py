@@ -28,7 +28,11 @@ class RmsNormFwdConfig:
     @classmethod
     def from_analytical_heuristic(cls, N: int, dtype_width: int, arch_major: Optional[int] = None,
                                   is_layernorm: bool = False) -> "RmsNormFwdConfig":
-        """The configuration the C launcher's heuristic picks for an aligned row of N elements."""
+        """The launch geometry of the C launcher's heuristic for an aligned row of N elements that
+        is held as fp32 registers (fp32 input, or any input with a residual).  Packed 16-bit rows
+        without a residual -- twice the elements per register -- are planned by the launcher with
+        up to 16 chunks per thread and 256-thread CTAs from N = 6144, which this value does not
+        describe; ``qb_last_kernel`` names the instantiation that actually ran."""
         vec = 128 // dtype_width
         threads, tpr, cluster_n = _plan(N, vec, pref_elems=16384 if vec == 8 else 8192,
                                         k_target=8, caps=(64, 32, 16), default_threads=128)
