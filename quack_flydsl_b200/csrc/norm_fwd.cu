@@ -445,20 +445,6 @@ extern "C" int qb_norm_fwd(const qb_norm_fwd_args* args, qb_stream_t stream) {
       overlaps(a.residual_out, a.residual_out_row_stride, a.residual, a.residual_row_stride, false) ||
       overlaps(a.out, a.out_row_stride, a.x, a.x_row_stride, true) ||
       overlaps(a.out, a.out_row_stride, a.residual, a.residual_row_stride, true);
-  if (uniform && a.H == 1 && a.cfg.cluster_n == 0 && !(a.cfg.flags & 2) && a.M >= dev->sm_count &&
-      !aliased && (long_row || (a.cfg.flags & 16))) {
-    // CTA sizes that exist: 256 and 512 threads (a caller's hint is rounded to one of them).
-    const int t = a.cfg.num_threads > 0 ? (a.cfg.num_threads > 256 ? 512 : 256)
-                                        : (a.residual != nullptr ? 512 : 256);
-    p.tpr = t;
-    p.rows_per_cta = 1;
-    p.cluster_n = 1;
-    p.cols_per_cta = static_cast<int>(a.N);
-    p.num_tiles = a.M;
-    p.stage_params = 0;
-    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    return launch_norm_fwd_stream_any(p, t, dev, st);
-  }
   // Per-thread capacity in row elements: fp32-held rows 64 (<= 512 threads) / 16 (1024 threads);
   // packed 16-bit rows twice that; the generic mixed-dtype path (wider staging registers) 32.
   RowPlan plan;
@@ -473,8 +459,38 @@ extern "C" int qb_norm_fwd(const qb_norm_fwd_args* args, qb_stream_t stream) {
   // LayerNorm, with its second pass over the registers, keeps 16 chunks: 5.88 against 4.40 TB/s.)
   const bool one_cta_row = raw && !a.is_layernorm && a.N * host_dtype_bytes(a.x_dtype) == 16384;
   const int k_target = (raw && !one_cta_row) ? 16 : 8;
-  if (int rc = plan_rows("norm_fwd", a.N, vec, caps, pref, k_target,
-                         raw && a.N >= 6144 && !one_cta_row ? 256 : 128, a.cfg, &plan))
+  const int default_threads = raw && a.N >= 6144 && !one_cta_row ? 256 : 128;
+  // RMSNorm rows that split evenly over a cluster stay on the register kernel: with the st.async
+  // exchange it beats the two-pass kernel at every long row measured (bf16, 512 MiB per tensor,
+  // without / with residual: N = 65536 5.36 / 6.04 against 4.91 / 5.65 TB/s, N = 131072 5.13 /
+  // 5.75 against 4.17 / 5.00, N = 262144 4.78 / 5.12 against 3.48 / 4.70).  Rows that would leave
+  // more than an eighth of the cluster's register tile empty (N = 40960: 4.55 against 5.13) and
+  // LayerNorm (whose parameters are not staged in the cluster kernel: 2.9 against 4.5) take the
+  // two-pass kernel.
+  bool prefer_cluster = false;
+  if (!a.is_layernorm && long_row && !(a.cfg.flags & 16)) {
+    RowPlan probe;
+    if (plan_rows("norm_fwd", a.N, vec, caps, pref, k_target, default_threads, qb_launch_cfg{}, &probe) == QB_OK) {
+      const int64_t tile = static_cast<int64_t>(probe.cluster_n) * probe.tpr * probe.K * vec;
+      prefer_cluster = tile > 0 && (tile - a.N) * 8 <= tile;
+    }
+    clear_error();
+  }
+  if (uniform && a.H == 1 && a.cfg.cluster_n == 0 && !(a.cfg.flags & 2) && a.M >= dev->sm_count &&
+      !aliased && !prefer_cluster && (long_row || (a.cfg.flags & 16))) {
+    // CTA sizes that exist: 256 and 512 threads (a caller's hint is rounded to one of them).
+    const int t = a.cfg.num_threads > 0 ? (a.cfg.num_threads > 256 ? 512 : 256)
+                                        : (a.residual != nullptr ? 512 : 256);
+    p.tpr = t;
+    p.rows_per_cta = 1;
+    p.cluster_n = 1;
+    p.cols_per_cta = static_cast<int>(a.N);
+    p.num_tiles = a.M;
+    p.stage_params = 0;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    return launch_norm_fwd_stream_any(p, t, dev, st);
+  }
+  if (int rc = plan_rows("norm_fwd", a.N, vec, caps, pref, k_target, default_threads, a.cfg, &plan))
     return rc;
   const int K = plan.K;
   const int threads = plan.threads;
