@@ -562,11 +562,16 @@ def sharded_suite(dev, rank, world, peak) -> dict:
     dloss = torch.full((M,), 1.0 / count, device=dev)
     state = {}
 
-    def ce_step(tl=None):
+    peer_ce = sharded.PeerAllReduce(dev, cap_cols=3 * M)
+
+    def ce_step(tl=None, fused=True):
         run = tl.run if tl is not None else (lambda _n, f: f())
         run("stats", lambda: state.__setitem__("stats", sharded.ce_shard_stats(xsh, target, c0)))
-        run("allgather", lambda: state.__setitem__("all", sharded.gather_ce_stats(state["stats"])))
-        run("combine", lambda: state.__setitem__("ll", sharded.ce_combine(state["all"], target)))
+        if fused:
+            run("exchange_combine", lambda: state.__setitem__("ll", peer_ce.ce_combine(state["stats"], target)))
+        else:
+            run("allgather", lambda: state.__setitem__("all", sharded.gather_ce_stats(state["stats"])))
+            run("combine", lambda: state.__setitem__("ll", sharded.ce_combine(state["all"], target)))
         run("bwd", lambda: state.__setitem__("dx", sharded.ce_shard_bwd(xsh, target, dloss, state["ll"][1], c0)))
 
     ce_step()
@@ -589,13 +594,31 @@ def sharded_suite(dev, rank, world, peak) -> dict:
     torch.cuda.synchronize()
     ms = max_ms(e0.elapsed_time(e1) / 10)
     phases = {k: round(max_ms(v), 4) for k, v in tl.median_ms().items()}
+    tl2 = Timeline()
+    for _ in range(2):
+        ce_step(fused=False)
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(10):
+        ce_step(tl2, fused=False)
+    e1.record()
+    torch.cuda.synchronize()
+    ms_nccl = max_ms(e0.elapsed_time(e1) / 10)
+    phases_nccl = {k: round(max_ms(v), 4) for k, v in tl2.median_ms().items()}
+    ce_timeouts = peer_ce.timeouts()
+    peer_ce.close()
     nbytes = (M * V * 2 + 16 * M) + (2 * M * V * 2 + 16 * M)  # forward + backward of the whole problem
     oks = torch.tensor([int(ok_ce), int(ok_ln)], device=dev)
     dist.all_reduce(oks, op=dist.ReduceOp.MIN)
     res["ce_vocab_sharded"] = {
         "shape": [M, V], "cols_per_rank": Ns, "ms": round(ms, 4), "gbs_aggregate": round(nbytes / ms / 1e6, 1),
         "frac_of_measured_peak": round(nbytes / ms / 1e6 / (peak * world), 4), "phases_ms": phases,
-        "collective": f"one NCCL all-gather of the (3, {M}) fp32 row statistics ({3 * M * 4 // 1024} KiB per rank)",
+        "collective": f"the (3, {M}) fp32 row statistics ({3 * M * 4 // 1024} KiB per rank) exchanged and folded by one "
+                      "kernel (peer stores + flags)",
+        "collective_timeouts": ce_timeouts,
+        "with_nccl_allgather": {"ms": round(ms_nccl, 4), "phases_ms": phases_nccl},
         "self_check": bool(oks[0])}
     res["layernorm_row_sharded"]["self_check"] = bool(oks[1]) if rank != 0 else (ok_ln and bool(oks[1]))
     return res

@@ -54,7 +54,9 @@ typedef struct qb_launch_cfg {
                               0 = heuristic */
   int32_t flags;           /* kernel-selection bits for tuning builds; 0 = heuristic (see the
                               QB_FLAG_* constants below) */
-  int32_t ctas_per_sm;     /* shared-memory ring kernels: CTAs that share one SM (1 or 2); 0 = heuristic */
+  int32_t ctas_per_sm;     /* shared-memory ring kernels: CTAs that share one SM (1 or 2); softmax
+                              cluster-register kernel: row buffers per thread (1 = no prefetch, 2, 3);
+                              0 = heuristic */
   int32_t reserved;
 } qb_launch_cfg;
 
@@ -242,6 +244,37 @@ typedef struct qb_colsum_allreduce_args {
 } qb_colsum_allreduce_args;
 
 int qb_colsum_allreduce(const qb_colsum_allreduce_args* args, qb_stream_t stream);
+
+/*
+ * Vocabulary-sharded cross-entropy: exchange of the per-row (max, sum-exp, target logit) between
+ * the GPUs of one node fused with their fold into (loss, lse) -- one launch instead of an
+ * all-gather of the (3, M) fp32 block followed by qb_ce_combine, same arithmetic and shard order
+ * as qb_ce_combine.  stats is this rank's (3, M) block; the exchange buffers, peers, seq and status
+ * are those of qb_colsum_allreduce (one step counter per set of buffers, shared by both entry
+ * points); needs 3 * M <= cap_cols and at most 262144 rows per launch.  No counterpart in the
+ * reference (single-GPU analogue: the lse_partial mode, quack/cross_entropy.py:676-694).
+ */
+typedef struct qb_ce_combine_exchange_args {
+  const float* stats;  /* (3, M) fp32 of this rank */
+  const void* target;
+  const void* weight;  /* optional */
+  float* loss;
+  float* lse;
+  void* peers[QB_MAX_PEERS];
+  uint32_t* status;
+  int64_t M;
+  int64_t cap_cols;
+  int64_t ignore_index;
+  int64_t num_classes;
+  int32_t target_dtype;
+  int32_t weight_dtype;
+  int32_t world;
+  int32_t rank;
+  uint32_t seq;
+  int32_t pad0;
+} qb_ce_combine_exchange_args;
+
+int qb_ce_combine_exchange(const qb_ce_combine_exchange_args* args, qb_stream_t stream);
 /* Bytes of one rank's exchange buffer for `world` ranks and cap_cols columns (-1: bad arguments). */
 int64_t qb_peer_buffer_bytes(int32_t world, int64_t cap_cols);
 int qb_peer_buffer_create(int32_t world, int64_t cap_cols, void** local, unsigned char* handle);
@@ -526,7 +559,8 @@ int qb_abi_version(void);
  * sizeof() of an argument block as compiled into the library, so a foreign-language binding can
  * verify its struct layout before the first call.  which: 0 launch_cfg, 1 norm_fwd, 2 norm_bwd,
  * 3 colsum, 4 softmax_fwd, 5 softmax_bwd, 6 ce_fwd, 7 ce_bwd, 8 ce_combine, 9 device_info,
- * 10 norm_bwd_static, 11 rms_final_reduce, 12 topk_fwd, 13 topk_bwd, 14 colsum_allreduce.
+ * 10 norm_bwd_static, 11 rms_final_reduce, 12 topk_fwd, 13 topk_bwd, 14 colsum_allreduce,
+ * 15 ce_combine_exchange.
  * Returns -1 for an unknown code.
  */
 int qb_sizeof_args(int32_t which);

@@ -112,6 +112,16 @@ class ColsumAllreduceArgs(Structure):
     ]
 
 
+class CeCombineExchangeArgs(Structure):
+    _fields_ = [
+        ("stats", c_void_p), ("target", c_void_p), ("weight", c_void_p), ("loss", c_void_p),
+        ("lse", c_void_p), ("peers", c_void_p * QB_MAX_PEERS), ("status", c_void_p),
+        ("M", c_int64), ("cap_cols", c_int64), ("ignore_index", c_int64), ("num_classes", c_int64),
+        ("target_dtype", c_int32), ("weight_dtype", c_int32), ("world", c_int32), ("rank", c_int32),
+        ("seq", ctypes.c_uint32), ("pad0", c_int32),
+    ]
+
+
 class SoftmaxFwdArgs(Structure):
     _fields_ = [
         ("x", c_void_p), ("out", c_void_p), ("M", c_int64), ("N", c_int64),
@@ -182,7 +192,7 @@ _SIZEOF_CODES = {
     0: LaunchCfg, 1: NormFwdArgs, 2: NormBwdArgs, 3: ColsumArgs, 4: SoftmaxFwdArgs,
     5: SoftmaxBwdArgs, 6: CeFwdArgs, 7: CeBwdArgs, 8: CeCombineArgs, 9: DeviceInfo,
     10: NormBwdStaticArgs, 11: RmsFinalReduceArgs, 12: TopkFwdArgs, 13: TopkBwdArgs,
-    14: ColsumAllreduceArgs,
+    14: ColsumAllreduceArgs, 15: CeCombineExchangeArgs,
 }
 
 # every symbol include/quack_b200.h declares
@@ -191,7 +201,7 @@ EXPORTED_SYMBOLS = (
     "qb_softmax_bwd", "qb_ce_fwd", "qb_ce_bwd", "qb_ce_combine", "qb_query_device",
     "qb_last_error", "qb_abi_version", "qb_sizeof_args", "qb_norm_bwd_static",
     "qb_rms_final_reduce", "qb_ring_timeouts", "qb_last_kernel", "qb_topk_fwd", "qb_topk_bwd",
-    "qb_colsum_allreduce", "qb_peer_buffer_bytes", "qb_peer_buffer_create", "qb_peer_buffer_open",
+    "qb_colsum_allreduce", "qb_ce_combine_exchange", "qb_peer_buffer_bytes", "qb_peer_buffer_create", "qb_peer_buffer_open",
     "qb_peer_buffer_close", "qb_peer_buffer_destroy",
 )
 
@@ -242,6 +252,7 @@ def lib() -> ctypes.CDLL:
         ("qb_norm_bwd_static", NormBwdStaticArgs), ("qb_rms_final_reduce", RmsFinalReduceArgs),
         ("qb_topk_fwd", TopkFwdArgs), ("qb_topk_bwd", TopkBwdArgs),
         ("qb_colsum_allreduce", ColsumAllreduceArgs),
+        ("qb_ce_combine_exchange", CeCombineExchangeArgs),
     ):
         fn = getattr(cdll, name)
         fn.restype = ctypes.c_int

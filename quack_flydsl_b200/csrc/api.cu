@@ -265,6 +265,7 @@ extern "C" int qb_sizeof_args(int32_t which) {
     case 12: return (int)sizeof(qb_topk_fwd_args);
     case 13: return (int)sizeof(qb_topk_bwd_args);
     case 14: return (int)sizeof(qb_colsum_allreduce_args);
+    case 15: return (int)sizeof(qb_ce_combine_exchange_args);
     default: return -1;
   }
 }

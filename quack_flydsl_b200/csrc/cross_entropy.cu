@@ -182,9 +182,11 @@ __global__ void __launch_bounds__(T, (T >= 1024) ? 1 : (1024 / T)) ce_fwd_dx_ker
     // ---- pass 1 ----
     float m = neg_inf(), s = 0.0f;
     ExpOffset off = exp_offset(m);
+    // The block's chunks live at row scope: the block pass 1 reads last is the one pass 2 starts
+    // with, so it stays in registers across the row reduction instead of being read again.
+    uint32_t r[U][4];
     auto pass1 = [&](auto full_tag, const char* q, int c0) {
       constexpr bool FULL = decltype(full_tag)::value;
-      uint32_t r[U][4];
 #pragma unroll
       for (int u = 0; u < U; ++u) ldg16_hint<!FULL>(r[u], q + u * kStep, c0 + u * T < nchunks, keep);
       float cm = neg_inf();
@@ -236,11 +238,13 @@ __global__ void __launch_bounds__(T, (T >= 1024) ? 1 : (1024 / T)) ce_fwd_dx_ker
     // ---- pass 2: dx, newest lines first ----
     off = exp_offset(lse);
     const float pscale = fast_exp2(off.lo) * gscale;
-    auto pass2 = [&](auto full_tag, const char* q, char* qo, int c0) {
+    auto pass2 = [&](auto full_tag, auto resident_tag, const char* q, char* qo, int c0) {
       constexpr bool FULL = decltype(full_tag)::value;
-      uint32_t r[U][4];
+      constexpr bool RESIDENT = decltype(resident_tag)::value;  // the chunks are still in r
+      if constexpr (!RESIDENT) {
 #pragma unroll
-      for (int u = 0; u < U; ++u) ldg16_hint<!FULL>(r[u], q + u * kStep, c0 + u * T < nchunks, drop);
+        for (int u = 0; u < U; ++u) ldg16_hint<!FULL>(r[u], q + u * kStep, c0 + u * T < nchunks, drop);
+      }
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         float v[VEC], d[VEC];
@@ -258,13 +262,14 @@ __global__ void __launch_bounds__(T, (T >= 1024) ? 1 : (1024 / T)) ce_fwd_dx_ker
     };
     {
       const int64_t end = static_cast<int64_t>(nfull) * kBlockBytes;
-      if (tail) pass2(std::false_type{}, xin + end, dxo + end, tail_c0);
+      if (tail) pass2(std::false_type{}, std::true_type{}, xin + end, dxo + end, tail_c0);
       const char* q = xin + end;
       char* qo = dxo + end;
       for (int b = nfull - 1; b >= 0; --b) {
         q -= kBlockBytes;
         qo -= kBlockBytes;
-        pass2(std::true_type{}, q, qo, b * (T * U) + g.t);
+        if (!tail && b == nfull - 1) pass2(std::true_type{}, std::true_type{}, q, qo, b * (T * U) + g.t);
+        else pass2(std::true_type{}, std::false_type{}, q, qo, b * (T * U) + g.t);
       }
     }
   }

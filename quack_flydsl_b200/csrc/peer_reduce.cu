@@ -134,9 +134,122 @@ __global__ void __launch_bounds__(256) colsum_allreduce_kernel(const PeerReduceP
   }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Vocabulary-sharded cross-entropy: exchange of the per-row statistics fused with their fold
+// ---------------------------------------------------------------------------------------------
+// Every rank holds (max, sum-exp, target logit) of its column slice for all M rows.  One block of
+// 256 threads owns 256 rows: it stores their three statistics into its slot of every rank's
+// exchange buffer, raises its flag there, waits (bounded) for the same block's flags from all
+// ranks and folds the G shards in rank order exactly as ce_combine_kernel does.  Replaces an
+// all-gather of the (3, M) block followed by ce_combine.  Slot of rank r, parity par:
+// data[(par * G + r) * cap_cols + k * M + row], k = 0 (max), 1 (sum-exp), 2 (target logit).
+struct CeExchangeParams {
+  qb_ce_combine_exchange_args a;
+};
+
+__device__ __forceinline__ bool peer_wait_flag(const uint32_t* f, uint32_t seq, uint32_t* status) {
+  auto reached = [&](uint32_t v) { return static_cast<int32_t>(v - seq) >= 0; };
+  if (reached(ld_acquire_sys_u32(f))) return true;
+  const unsigned long long t0 = peer_timer_ns();
+  for (;;) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i) {
+      if (reached(ld_acquire_sys_u32(f))) return true;
+      __nanosleep(64);
+    }
+    if (peer_timer_ns() - t0 > kPeerTimeoutNs) {
+      if (status != nullptr) atomicAdd(status, 1u);
+      return false;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) ce_combine_exchange_kernel(const CeExchangeParams p) {
+  const qb_ce_combine_exchange_args& a = p.a;
+  const int tid = threadIdx.x;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 256 + tid;
+  const bool live = row < a.M;
+  const int G = a.world;
+  const uint32_t par = a.seq & 1u;
+  const int64_t cap_cols = a.cap_cols;
+  const int64_t cap_blocks = cap_cols / 32;
+  const int64_t data_words = 2 * static_cast<int64_t>(G) * cap_cols;
+  const int64_t slot = (static_cast<int64_t>(par) * G + a.rank) * cap_cols;
+  if (live) {
+    const float m = a.stats[row], s = a.stats[a.M + row], t = a.stats[2 * a.M + row];
+    for (int r = 0; r < G; ++r) {
+      float* data = reinterpret_cast<float*>(a.peers[r]) + slot;
+      data[row] = m;
+      data[a.M + row] = s;
+      data[2 * a.M + row] = t;
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (tid < G) {
+    uint32_t* flags = reinterpret_cast<uint32_t*>(a.peers[tid]) + data_words;
+    st_release_sys_u32(&flags[(static_cast<int64_t>(par) * G + a.rank) * cap_blocks + blockIdx.x], a.seq);
+    const uint32_t* mine = reinterpret_cast<const uint32_t*>(a.peers[a.rank]) + data_words;
+    peer_wait_flag(&mine[(static_cast<int64_t>(par) * G + tid) * cap_blocks + blockIdx.x], a.seq, a.status);
+  }
+  __syncthreads();
+  if (!live) return;
+  const float* mine = reinterpret_cast<const float*>(a.peers[a.rank]);
+  float m = neg_inf();
+  for (int g = 0; g < G; ++g)
+    m = fmaxf(m, ld_relaxed_sys_f32(&mine[(static_cast<int64_t>(par) * G + g) * cap_cols + row]));
+  float s = 0.0f, t = 0.0f;
+  for (int g = 0; g < G; ++g) {
+    const float* sl = mine + (static_cast<int64_t>(par) * G + g) * cap_cols;
+    const float mg = ld_relaxed_sys_f32(&sl[row]);
+    const float sg = ld_relaxed_sys_f32(&sl[a.M + row]);
+    if (mg != neg_inf()) s += sg * exp2f((mg - m) * kLog2e);
+    t += ld_relaxed_sys_f32(&sl[2 * a.M + row]);
+  }
+  const float log_s = logf(s);
+  if (a.lse != nullptr) a.lse[row] = m + log_s;
+  if (a.loss != nullptr) {
+    const int64_t tgt = load_index(a.target, row, a.target_dtype);
+    const bool ignored = tgt == a.ignore_index || tgt < 0 || (a.num_classes > 0 && tgt >= a.num_classes);
+    float wt = 1.0f;
+    if (a.weight != nullptr && !ignored) wt = load_scalar(a.weight, tgt, a.weight_dtype);
+    a.loss[row] = ignored ? 0.0f : wt * ((m - t) + log_s);
+  }
+}
+
 }  // namespace qb
 
 using namespace qb;
+
+extern "C" int qb_ce_combine_exchange(const qb_ce_combine_exchange_args* args, qb_stream_t stream) {
+  clear_error();
+  if (args == nullptr) return set_error(QB_ERR_INVALID, "ce_combine_exchange: null argument block");
+  const qb_ce_combine_exchange_args& a = *args;
+  if (a.stats == nullptr || (a.loss == nullptr && a.lse == nullptr))
+    return set_error(QB_ERR_INVALID, "ce_combine_exchange: stats and an output are required");
+  if (a.loss != nullptr && a.target == nullptr)
+    return set_error(QB_ERR_INVALID, "ce_combine_exchange: the loss needs the targets");
+  if (a.M < 0) return set_error(QB_ERR_INVALID, "ce_combine_exchange: bad sizes");
+  if (a.world < 1 || a.world > QB_MAX_PEERS || a.rank < 0 || a.rank >= a.world)
+    return set_error(QB_ERR_INVALID, "ce_combine_exchange: bad rank %d of %d", a.rank, a.world);
+  if (a.seq == 0) return set_error(QB_ERR_INVALID, "ce_combine_exchange: step numbers start at 1");
+  const int64_t blocks = ceil_div(a.M, 256);
+  if (a.cap_cols <= 0 || a.cap_cols % 32 != 0 || 3 * a.M > a.cap_cols || blocks > a.cap_cols / 32)
+    return set_error(QB_ERR_UNSUPPORTED, "ce_combine_exchange: %lld rows exceed the exchange buffer (%lld words)",
+                     (long long)a.M, (long long)a.cap_cols);
+  if (blocks > 1024)  // all blocks wait for their peers: they have to be resident together
+    return set_error(QB_ERR_UNSUPPORTED, "ce_combine_exchange: more than 262144 rows per launch");
+  for (int r = 0; r < a.world; ++r)
+    if (a.peers[r] == nullptr) return set_error(QB_ERR_INVALID, "ce_combine_exchange: peer %d is not mapped", r);
+  if (a.loss != nullptr && a.target_dtype != QB_I32 && a.target_dtype != QB_I64)
+    return set_error(QB_ERR_INVALID, "ce_combine_exchange: unsupported target dtype");
+  if (a.M == 0) return QB_OK;
+  CeExchangeParams p;
+  p.a = a;
+  dim3 grid(static_cast<unsigned>(blocks), 1, 1);
+  return launch_kernel(ce_combine_exchange_kernel, grid, 256, 0, 1, reinterpret_cast<cudaStream_t>(stream), p,
+                       "ce_combine_exchange");
+}
 
 extern "C" int64_t qb_peer_buffer_bytes(int32_t world, int64_t cap_cols) {
   if (world <= 0 || world > QB_MAX_PEERS || cap_cols <= 0 || cap_cols % 32 != 0) return -1;

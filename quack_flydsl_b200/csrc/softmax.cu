@@ -226,11 +226,16 @@ __global__ void __launch_bounds__(T, (T >= 1024) ? 1 : (1024 / T)) softmax_strea
 #pragma unroll
     for (int i = 0; i < (BWD ? VEC : 1); ++i) sv[i] = 0.0f;
 
+    // The block's chunks live at row scope: the block pass 1 reads last is the one pass 2 starts
+    // with, so it is kept in registers across the row reduction instead of being read again
+    // (rows of two blocks, e.g. N = 131072 with 1024 threads: a quarter less L2 traffic and one
+    // load latency less per row).
+    uint32_t r0[U][4];
+    uint32_t r1[BWD ? U : 1][4];
+
     // ---- pass 1 ----
     auto pass1 = [&](auto full_tag, const char* q0, const char* q1, int c0) {
       constexpr bool FULL = decltype(full_tag)::value;
-      uint32_t r0[U][4];
-      uint32_t r1[BWD ? U : 1][4];
 #pragma unroll
       for (int u = 0; u < U; ++u) ldg16_hint<!FULL>(r0[u], q0 + u * kStep, c0 + u * T < nchunks, keep);
       if constexpr (BWD) {
@@ -296,15 +301,16 @@ __global__ void __launch_bounds__(T, (T >= 1024) ? 1 : (1024 / T)) softmax_strea
     ++rit;
 
     // ---- pass 2: newest lines first ----
-    auto pass2 = [&](auto full_tag, const char* q0, const char* q1, char* qo, int c0) {
+    auto pass2 = [&](auto full_tag, auto resident_tag, const char* q0, const char* q1, char* qo, int c0) {
       constexpr bool FULL = decltype(full_tag)::value;
-      uint32_t r0[U][4];
-      uint32_t r1[BWD ? U : 1][4];
+      constexpr bool RESIDENT = decltype(resident_tag)::value;  // the chunks are still in r0 / r1
+      if constexpr (!RESIDENT) {
 #pragma unroll
-      for (int u = 0; u < U; ++u) ldg16_hint<!FULL>(r0[u], q0 + u * kStep, c0 + u * T < nchunks, drop);
-      if constexpr (BWD) {
+        for (int u = 0; u < U; ++u) ldg16_hint<!FULL>(r0[u], q0 + u * kStep, c0 + u * T < nchunks, drop);
+        if constexpr (BWD) {
 #pragma unroll
-        for (int u = 0; u < U; ++u) ldg16_hint<!FULL>(r1[u], q1 + u * kStep, c0 + u * T < nchunks, drop);
+          for (int u = 0; u < U; ++u) ldg16_hint<!FULL>(r1[u], q1 + u * kStep, c0 + u * T < nchunks, drop);
+        }
       }
 #pragma unroll
       for (int u = 0; u < U; ++u) {
@@ -326,7 +332,7 @@ __global__ void __launch_bounds__(T, (T >= 1024) ? 1 : (1024 / T)) softmax_strea
     };
     {
       const int64_t end = static_cast<int64_t>(nfull) * kBlockBytes;
-      if (tail) pass2(std::false_type{}, in0 + end, in1 + end, out + end, tail_c0);
+      if (tail) pass2(std::false_type{}, std::true_type{}, in0 + end, in1 + end, out + end, tail_c0);
       const char* q0 = in0 + end;
       const char* q1 = in1 + end;
       char* qo = out + end;
@@ -334,7 +340,8 @@ __global__ void __launch_bounds__(T, (T >= 1024) ? 1 : (1024 / T)) softmax_strea
         q0 -= kBlockBytes;
         q1 -= kBlockBytes;
         qo -= kBlockBytes;
-        pass2(std::true_type{}, q0, q1, qo, 0);
+        if (!tail && b == nfull - 1) pass2(std::true_type{}, std::true_type{}, q0, q1, qo, 0);
+        else pass2(std::true_type{}, std::false_type{}, q0, q1, qo, 0);
       }
     }
   }

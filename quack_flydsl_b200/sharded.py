@@ -140,6 +140,36 @@ class PeerAllReduce:
         a.world, a.rank, a.seq = self.world, self.rank, self.seq
         _C.launch(_C.lib().qb_colsum_allreduce, a, p0, "colsum_allreduce")
 
+    def ce_combine(self, stats: Tensor, target: Tensor, weight: Optional[Tensor] = None,
+                   ignore_index: int = -100) -> Tuple[Tensor, Tensor]:
+        """Vocabulary-sharded cross-entropy: exchanges this rank's (3, M) fp32 statistics with all
+        ranks and folds them in rank order into (loss, lse), both fp32 (M,), in one kernel
+        (``qb_ce_combine_exchange``) -- instead of ``gather_ce_stats`` + ``ce_combine``."""
+        assert stats.dtype == torch.float32 and stats.dim() == 2 and stats.shape[0] == 3
+        M = stats.shape[1]
+        loss = torch.empty(M, device=stats.device, dtype=torch.float32)
+        lse = torch.empty(M, device=stats.device, dtype=torch.float32)
+        if M == 0:
+            return loss, lse
+        s_ = stats.contiguous()
+        t_ = target.contiguous()
+        w_ = weight.contiguous() if weight is not None else None
+        self.seq += 1
+        a = _C.CeCombineExchangeArgs()
+        a.stats, a.target, a.weight = _C.ptr(s_), _C.ptr(t_), _C.ptr(w_)
+        a.loss, a.lse = _C.ptr(loss), _C.ptr(lse)
+        for r in range(self.world):
+            a.peers[r] = self._peers[r]
+        a.status = self.status.data_ptr()
+        a.M, a.cap_cols = M, self.cap_cols
+        a.ignore_index = int(ignore_index)
+        a.num_classes = w_.numel() if w_ is not None else 0
+        a.target_dtype = _C.INDEX_CODES[t_.dtype]
+        a.weight_dtype = _C.float_code(w_)
+        a.world, a.rank, a.seq = self.world, self.rank, self.seq
+        _C.launch(_C.lib().qb_ce_combine_exchange, a, s_, "ce_combine_exchange")
+        return loss, lse
+
     def timeouts(self) -> int:
         """Waits that gave up (0 in a healthy job); synchronises."""
         return int(self.status.item())
@@ -306,10 +336,14 @@ class VocabParallelCrossEntropy(torch.autograd.Function):
     """Per-row loss of logits whose vocabulary dimension is split over the ranks of ``group``."""
 
     @staticmethod
-    def forward(ctx, x_shard, target, col_offset, weight, ignore_index, group, inplace_backward):
+    def forward(ctx, x_shard, target, col_offset, weight, ignore_index, group, inplace_backward,
+                peer=None):
         stats = ce_shard_stats(x_shard, target, col_offset, ignore_index)
-        stats_all = gather_ce_stats(stats, group)
-        loss, lse = ce_combine(stats_all, target, weight, ignore_index)
+        if peer is not None:
+            loss, lse = peer.ce_combine(stats, target, weight, ignore_index)
+        else:
+            stats_all = gather_ce_stats(stats, group)
+            loss, lse = ce_combine(stats_all, target, weight, ignore_index)
         ctx.save_for_backward(x_shard, target, lse, weight)
         ctx.col_offset, ctx.ignore_index, ctx.inplace = col_offset, ignore_index, inplace_backward
         return loss
@@ -319,17 +353,19 @@ class VocabParallelCrossEntropy(torch.autograd.Function):
         x_shard, target, lse, weight = ctx.saved_tensors
         dx = ce_shard_bwd(x_shard, target, dloss, lse, ctx.col_offset, weight, ctx.ignore_index,
                           inplace=ctx.inplace)
-        return dx, None, None, None, None, None, None
+        return dx, None, None, None, None, None, None, None
 
 
 def cross_entropy_vocab_parallel(x_shard: Tensor, target: Tensor, col_offset: int,
                                  weight: Optional[Tensor] = None, ignore_index: int = -100,
                                  reduction: str = "mean", group=None,
-                                 inplace_backward: bool = False) -> Tensor:
+                                 inplace_backward: bool = False, peer=None) -> Tensor:
     """Cross-entropy over vocabulary-sharded logits.  ``target`` holds global class ids and is
-    replicated; ``col_offset`` is the global id of this rank's first column."""
+    replicated; ``col_offset`` is the global id of this rank's first column.  ``peer``: a
+    ``PeerAllReduce`` of the group whose buffers hold 3 * M words; the exchange of the row
+    statistics and their fold then run as one kernel instead of an all-gather + combine."""
     loss = VocabParallelCrossEntropy.apply(x_shard, target, col_offset, weight, ignore_index,
-                                           group, inplace_backward)
+                                           group, inplace_backward, peer)
     if reduction == "none":
         return loss
     if reduction == "sum":

@@ -68,6 +68,22 @@ def main():
     ok &= par.timeouts() == 0
     par.close()
 
+    # The fused exchange + fold of the vocabulary-sharded row statistics against all-gather +
+    # ce_combine: bit-identical loss and lse on every rank, several steps on one set of buffers.
+    Ms = 3000
+    pce = sharded.PeerAllReduce(dev, cap_cols=3 * Ms + 32)
+    gc = torch.Generator(device=dev).manual_seed(7)
+    tgt = torch.randint(0, 100, (Ms,), device=dev, generator=gc)
+    tgt[::11] = -100
+    for step in range(4):
+        st = torch.randn(3, Ms, device=dev, generator=gp)
+        st[1].abs_().add_(0.25)
+        loss_f, lse_f = pce.ce_combine(st, tgt)
+        loss_r, lse_r = sharded.ce_combine(sharded.gather_ce_stats(st), tgt)
+        ok &= torch.equal(loss_f, loss_r) and torch.equal(lse_f, lse_r)
+    ok &= pce.timeouts() == 0
+    pce.close()
+
     Mc, Nc = 256, 128256
     logits = (2 * torch.randn(Mc, Nc, generator=g)).bfloat16()
     target = torch.randint(0, Nc, (Mc,), generator=g)

@@ -146,6 +146,34 @@ def test_peer_allreduce_single_rank_equals_column_sum():
 
 
 @pytest.mark.gpu
+def test_peer_ce_combine_single_rank_equals_ce_combine():
+    """With one rank the fused exchange + fold must reproduce qb_ce_combine bit for bit (ignored
+    rows, class weights, a row whose shard is all -inf), repeatedly on the same buffers."""
+    dev = torch.device("cuda", 0)
+    par = sharded.PeerAllReduce(dev, cap_cols=3 * 1000 + 8)
+    try:
+        for M in (1000, 1, 257):
+            stats = torch.randn(3, M, device=dev)
+            stats[1].abs_().add_(0.5)
+            if M > 5:
+                stats[0, 5] = float("-inf")
+                stats[1, 5] = 0.0
+            V = 50
+            target = torch.randint(0, V, (M,), device=dev)
+            target[::7] = -100
+            w = torch.rand(V, device=dev) + 0.5
+            for weight in (None, w):
+                loss, lse = par.ce_combine(stats, target, weight)
+                loss2, lse2 = sharded.ce_combine(stats[None], target, weight)
+                assert torch.equal(loss, loss2) and torch.equal(lse.nan_to_num(), lse2.nan_to_num())
+        with pytest.raises(ValueError, match="exceed the exchange buffer"):
+            par.ce_combine(torch.randn(3, 2000, device=dev), torch.zeros(2000, device=dev, dtype=torch.long))
+        assert par.timeouts() == 0
+    finally:
+        par.close()
+
+
+@pytest.mark.gpu
 def test_multi_gpu_nccl_paths():
     """Launches tests/_dist_worker.py under torchrun on 2 GPUs, as the reference does for its own
     distributed tests (tests/test_distributed_gemm.py:363-389)."""

@@ -143,3 +143,63 @@ def test_softmax_streamed_long_rows_match_cluster_path(dtype, monkeypatch):
         monkeypatch.delenv("QUACK_B200_CFG")
         assert_close_to_oracle(y, ref, dtype, atol=TOL[dtype], rtol=TOL[dtype], what="y")
         assert_close_to_oracle(dx, dx_ref, dtype, atol=TOL[dtype], rtol=TOL[dtype], max_ulp=None, what="dx")
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_softmax_cluster_register_kernel_variants(dtype, monkeypatch):
+    """Long rows split over a thread-block cluster with the slices held in registers
+    (softmax_cluster.cu): every instantiated geometry -- small CTAs without prefetch, large CTAs
+    with the next row in flight, the three-buffer pipeline, cluster sizes that are not powers of
+    two (N = 40960 -> 5 CTAs), a ragged last slice, fewer rows than clusters -- against the
+    oracle, forward and backward, and bit-identical results from run to run."""
+    from quack_flydsl_b200 import _C
+
+    flag = 128  # QB_FLAG_CLUSTER_REGS
+    fwd_cfgs = ["128:0:0:0:16:{f}:1", "256:0:0:0:8:{f}:1", "512:0:0:0:4:{f}:2", "1024:0:0:0:2:{f}:2",
+                "512:0:0:0:2:{f}:3", "256:0:0:0:8:{f}:2"]
+    bwd_cfgs = ["128:0:0:0:8:{f}:1", "256:0:0:0:4:{f}:1", "512:0:0:0:2:{f}:2", "1024:0:0:0:2:{f}:2",
+                "256:0:0:0:2:{f}:3", "512:0:0:0:4:{f}:2"]
+    for M, N in [(150, 65536), (301, 40960), (149, 40008), (200, 32768 + 8)]:
+        x = (3.0 * torch.randn(M, N, device=DEV)).to(dtype)
+        x[1, 100:] = float("-inf")
+        dy = torch.randn(M, N, device=DEV).to(dtype)
+        ref = oracle.softmax_ref(x.cpu().float())
+        y0 = sm.softmax_fwd(x)
+        dx_ref = oracle.softmax_bwd_ref(dy.cpu().float(), y0.cpu().float())
+        ran = 0
+        for c in fwd_cfgs:
+            monkeypatch.setenv("QUACK_B200_CFG", "softmax_fwd:" + c.format(f=flag))
+            y = torch.full_like(x, float("nan"))
+            try:
+                sm._softmax_fwd(x, y)
+            except ValueError:
+                continue  # the geometry cannot hold this row (more than 16 CTAs)
+            finally:
+                monkeypatch.delenv("QUACK_B200_CFG")
+            if "softmax_cluster_kernel" not in _C.last_kernel():
+                continue  # fell through to another kernel: capacity
+            ran += 1
+            assert_close_to_oracle(y, ref, dtype, atol=TOL[dtype], rtol=TOL[dtype], what=f"y {c} {M}x{N}")
+            assert (y[1, 100:] == 0).all()
+        for c in bwd_cfgs:
+            monkeypatch.setenv("QUACK_B200_CFG", "softmax_bwd:" + c.format(f=flag))
+            dx = torch.full_like(x, float("nan"))
+            dx2 = torch.full_like(x, float("nan"))
+            try:
+                sm._softmax_backward(dy, y0, dx)
+                sm._softmax_backward(dy, y0, dx2)
+            except ValueError:
+                continue
+            finally:
+                monkeypatch.delenv("QUACK_B200_CFG")
+            if "softmax_cluster_kernel" not in _C.last_kernel():
+                continue
+            ran += 1
+            assert_close_to_oracle(dx, dx_ref, dtype, atol=TOL[dtype], rtol=TOL[dtype], max_ulp=None,
+                                   what=f"dx {c} {M}x{N}")
+            assert torch.equal(dx, dx2)
+        assert ran >= 4, f"the cluster kernel did not serve {M}x{N} {dtype}"
+    # the default backward for long rows is this kernel; no wait may have timed out
+    dx = sm.softmax_bwd(dy, y0)
+    assert "softmax_cluster_kernel" in _C.last_kernel()
+    assert _C.ring_timeouts() == 0
