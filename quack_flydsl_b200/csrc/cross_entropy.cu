@@ -58,7 +58,46 @@ __global__ void __launch_bounds__(512) ce_fwd_kernel(const CeFwdParams p) {
     float m = neg_inf();
     float s = 0.0f;
     ExpOffset off = exp_offset(m);
-    for (int c = g.t; c < nchunks; c += p.tpr * kCeUnroll) {
+    int c = g.t;
+    if constexpr (DT != kDynDT) {
+      // Blocks of kCeUnroll chunks that lie completely inside the row: unpredicated loads through
+      // one byte pointer, the block's maximum first (packed for 16-bit dtypes) and one re-basing
+      // check per block instead of one per chunk.
+      constexpr int kEsz = DT == QB_F32 ? 4 : 2;
+      const int step = p.tpr * VEC * kEsz;
+      const char* xp = reinterpret_cast<const char*>(a.x) + (xrow + static_cast<int64_t>(c) * VEC) * kEsz;
+      for (; row_ok && c + (kCeUnroll - 1) * p.tpr < nchunks; c += p.tpr * kCeUnroll, xp += step * kCeUnroll) {
+        uint32_t raw[kCeUnroll][RawWords<DT, VEC>::value];
+#pragma unroll
+        for (int u = 0; u < kCeUnroll; ++u) ldg_stream_full<VEC * kEsz>(raw[u], xp + u * step);
+        float cm;
+        if constexpr (DT == QB_F32) {
+          cm = __uint_as_float(raw[0][0]);
+#pragma unroll
+          for (int u = 0; u < kCeUnroll; ++u)
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) cm = fmaxf(cm, __uint_as_float(raw[u][i]));
+        } else {
+          cm = packed_max16<DT, VEC>(raw[0]);
+#pragma unroll
+          for (int u = 1; u < kCeUnroll; ++u) cm = fmaxf(cm, packed_max16<DT, VEC>(raw[u]));
+        }
+        if (cm > m) {
+          const ExpOffset nw = exp_offset(cm);
+          s *= fast_exp2(nw.hi - off.hi);
+          m = cm;
+          off = nw;
+        }
+#pragma unroll
+        for (int u = 0; u < kCeUnroll; ++u) {
+          float v[VEC];
+          unpack_chunk<DT, VEC>(v, raw[u], DT);
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) s += fast_exp2(fmaf(v[i], kLog2e, off.hi));
+        }
+      }
+    }
+    for (; c < nchunks; c += p.tpr * kCeUnroll) {
       uint32_t raw[kCeUnroll][RawWords<DT, VEC>::value];
 #pragma unroll
       for (int u = 0; u < kCeUnroll; ++u) {

@@ -136,6 +136,8 @@ norm_fwd_kernel(const NormFwdParams p) {
     constexpr int kRawWords = RawWords<DT, VEC>::value;
     uint32_t rx[RAW ? K : 1][kRawWords];
     float v[RAW ? 1 : K][VEC];
+    // (Predicated loads also for full rows: the unpredicated form of load_row_raw, which gains
+    // 5 % in the softmax forward, measured 3 % / 7 % slower here for RMSNorm / LayerNorm.)
     if constexpr (RAW) {
 #pragma unroll
       for (int k = 0; k < K; ++k)

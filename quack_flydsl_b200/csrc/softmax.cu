@@ -51,9 +51,7 @@ softmax_fwd_kernel(const SoftmaxParams p) {
     const char* xp = reinterpret_cast<const char*>(p.in0) + (row * p.ld0 + colbase) * esz_i;
     char* op = reinterpret_cast<char*>(p.out) + (row * p.ldo + colbase) * esz_o;
     const int step_i = cstride * esz_i, step_o = cstride * esz_o;
-#pragma unroll
-    for (int k = 0; k < K; ++k)
-      load_chunk_raw_p<DT, VEC>(rx[k], xp + k * step_i, p.dt0, k < nkr);
+    load_row_raw<DT, VEC, K>(rx, xp, step_i, p.dt0, nkr);
 
     // Thread-local maximum over the chunks that exist.
     float m_t = neg_inf();
@@ -153,10 +151,8 @@ softmax_bwd_kernel(const SoftmaxParams p) {
     const char* yp = reinterpret_cast<const char*>(p.in1) + (row * p.ld1 + colbase) * esz1;
     char* op = reinterpret_cast<char*>(p.out) + (row * p.ldo + colbase) * esz_o;
     const int step0 = cstride * esz0, step1 = cstride * esz1, step_o = cstride * esz_o;
-#pragma unroll
-    for (int k = 0; k < K; ++k) load_chunk_raw_p<DT, VEC>(rdy[k], dyp + k * step0, p.dt0, k < nkr);
-#pragma unroll
-    for (int k = 0; k < K; ++k) load_chunk_raw_p<DT, VEC>(ry[k], yp + k * step1, p.dt1, k < nkr);
+    load_row_raw<DT, VEC, K>(rdy, dyp, step0, p.dt0, nkr);
+    load_row_raw<DT, VEC, K>(ry, yp, step1, p.dt1, nkr);
     float dot = 0.0f;
 #pragma unroll
     for (int k = 0; k < K; ++k) {

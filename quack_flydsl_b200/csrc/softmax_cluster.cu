@@ -14,8 +14,8 @@
 // mbarrier of that peer (the reference's store_shared_remote + mbarrier pair, quack/utils.py:27-58).
 // barrier.cluster is not used inside the row loop: its arrive has release semantics, which makes
 // the thread wait for its global loads in flight -- exactly the prefetched rows (measured: 4.0
-// instead of 5.9 TB/s at N = 65536).  Every mbarrier wait is bounded (ring.cuh): a wait that does
-// not succeed within two seconds sets the CTA's abort flag and bumps the device-side counter the
+// instead of 5.9 TB/s at N = 65536).  Every mbarrier wait is bounded (bounded_mbar_wait): a wait that
+// does not succeed within about a second sets the CTA's abort flag and bumps the device-side counter the
 // host reads, and the kernel runs to its end instead of hanging.
 // Loads in this file use the default L2 policy instead of the evict-first "streaming" one:
 // measured on B200, evict-first loads lose 1-3 % here whenever L2 still holds lines that other
@@ -36,26 +36,6 @@ struct __align__(16) ClusterScratch {
   float2 warp_part[2][kMaxWarps];   // per-warp partials of this CTA, by row parity
   int abort;                        // set once a wait of this CTA timed out
 };
-
-// Bounded wait on a local mbarrier (see ring_wait).
-__device__ __forceinline__ void cluster_row_wait(ClusterScratch* sc, uint32_t bar, uint32_t parity,
-                                                 unsigned int* timeouts) {
-  if (mbar_try_wait(bar, parity) != 0) return;
-  volatile int* ab = &sc->abort;
-  if (*ab) return;
-  const unsigned long long t0 = global_timer_ns();
-  for (;;) {
-#pragma unroll 1
-    for (int i = 0; i < 32; ++i)
-      if (mbar_try_wait(bar, parity) != 0) return;
-    if (*ab) return;
-    if (global_timer_ns() - t0 > kRingTimeoutNs) {
-      *ab = 1;
-      if (timeouts != nullptr) atomicAdd(timeouts, 1u);
-      return;
-    }
-  }
-}
 
 struct SoftmaxClusterParams {
   SoftmaxParams s;
@@ -219,7 +199,7 @@ softmax_cluster_kernel(const SoftmaxClusterParams q) {
   };
   auto wait_row = [&](int64_t j) {
     if (cn > 1)
-      cluster_row_wait(&sc, smem_u32(&sc.bar[j & 1]), static_cast<uint32_t>(j >> 1) & 1u, q.timeouts);
+      bounded_mbar_wait(&sc.abort, smem_u32(&sc.bar[j & 1]), static_cast<uint32_t>(j >> 1) & 1u, q.timeouts);
   };
   // every thread folds the cluster's partials in rank order (bit-identical in all CTAs)
   auto fold = [&](int par) -> float2 {
