@@ -316,6 +316,36 @@ def time_kernel(fn, iters=20, warmup=3):
     return statistics.median(a.elapsed_time(b) for a, b in pairs)
 
 
+def time_kernel_graph(fn, launches=20, replays=7):
+    """Median device time of fn() in ms with `launches` back-to-back launches captured in one CUDA
+    graph and the graph replayed `replays` times (the timing protocol of the reference's
+    quack/bench/bench_utils.py:69-155: no host launch path between the kernels; the tensors exceed
+    L2, so every launch starts L2-cold with respect to its own inputs).  None if capture fails."""
+    try:
+        for _ in range(3):
+            fn()  # fills every lazy host-side cache (occupancy, kernel attributes) before the capture
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(launches):
+                fn()
+        graph.replay()  # warm
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(replays):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            graph.replay()
+            b.record()
+            torch.cuda.synchronize()
+            times.append(a.elapsed_time(b) / launches)
+        del graph
+        return statistics.median(times)
+    except Exception:
+        torch.cuda.synchronize()
+        return None
+
+
 def copy_canary(dev) -> float:
     """The measurement behind MEASURED_PEAKS.json (b.copy_(a) over 1 Gi bf16 elements, read + write
     bytes, best of 10), repeated in this run: a contention / clock canary."""
@@ -389,6 +419,10 @@ def suite(dev, peak, cpu) -> dict:
     def timed(name, fn, nbytes, iters=20):
         ms = time_kernel(fn, iters=iters)
         rec(name, ms, nbytes, _C.last_kernel())
+        ms_g = time_kernel_graph(fn)
+        if ms_g is not None:
+            res[name]["cuda_graph"] = {"ms": round(ms_g, 4), "gbs": round(nbytes / ms_g / 1e6, 1),
+                                       "protocol": "20 launches in one CUDA graph, median of 7 replays"}
 
     g = torch.Generator(device=dev).manual_seed(1)
     bf = torch.bfloat16
@@ -757,9 +791,14 @@ def run_ours(args) -> None:
     # NCCL all-reduce on a side stream that overlaps the next step's forward).
     use_peer = world > 1 and args.collective == "peer"
     peer = None
+    peer_error = None
     if use_peer:
         from quack_flydsl_b200 import sharded as _sharded
-        peer = _sharded.PeerAllReduce(dev, cap_cols=N)
+        try:
+            peer = _sharded.PeerAllReduce(dev, cap_cols=N)
+        except RuntimeError as exc:  # raised on every rank together: all take the NCCL form instead
+            peer_error, use_peer = repr(exc), False
+            args.collective = "nccl"
     s_ar = torch.cuda.Stream(device=dev) if (world > 1 and args.collective != "none") else None
     ar_done = [None, None]
     counter = {"i": 0}
@@ -853,6 +892,17 @@ def run_ours(args) -> None:
     value = world * step_bytes / ms_step / 1e6
     kms = tl.median_ms()
     launches_per_step = 3  # forward, backward stage 1, column sum (the all-reduce is NCCL's)
+
+    # the same step and its two main kernels with the host launch path taken out (one GPU only)
+    graph_ms = None
+    if world == 1:
+        graph_ms = {
+            "step": time_kernel_graph(lambda: step(False), launches=20),
+            "rmsnorm_fwd": time_kernel_graph(
+                lambda: rn._rmsnorm_fwd(x, w, out, None, rstd, None, res, res_out, EPS)),
+            "rmsnorm_bwd": time_kernel_graph(
+                lambda: rn._rmsnorm_bwd(res_out, w, dout, rstd, dx, dw_partial, None, None, None, P)),
+        }
 
     # ---- strong scaling: the same [32768, 8192] problem split over the ranks ----
     strong = None
@@ -1056,6 +1106,8 @@ def run_ours(args) -> None:
         elif world > 1 and args.collective == "nccl":
             detail["kernels"] += (" + NCCL all-reduce of fp32 dw on a side stream, overlapping the next step's forward")
             detail["collective"] = "NCCL all-reduce"
+            if peer_error:
+                detail["collective_fallback_reason"] = peer_error
         elif world > 1:
             detail["collective"] = "none (diagnostic run)"
         mhz = clocks.get("sm_mhz") if clocks else None
@@ -1069,7 +1121,18 @@ def run_ours(args) -> None:
             "timing": {"blocks": len(blocks), "block_ms_median": round(ms_block, 4),
                        "block_ms_min": round(min(blocks), 4), "block_ms_max": round(max(blocks), 4),
                        "rule": f"blocks of {args.steps} steps repeated for >= {MIN_TIMED_SECONDS} s; median block",
-                       "ms_per_step_x_sm_mhz": round(ms_step * mhz, 2) if mhz else None},
+                       "ms_per_step_x_sm_mhz": round(ms_step * mhz, 2) if mhz else None,
+                       "cuda_graph": None if not graph_ms or graph_ms["step"] is None else {
+                           "protocol": "20 steps (fwd + bwd + column sum) or 20 launches of one kernel captured "
+                                       "in one CUDA graph, median of 7 replays",
+                           "ms_per_step": round(graph_ms["step"], 4),
+                           "value": round(step_bytes / graph_ms["step"] / 1e6, 1),
+                           "rmsnorm_fwd_ms": graph_ms["rmsnorm_fwd"] and round(graph_ms["rmsnorm_fwd"], 4),
+                           "rmsnorm_fwd_gbs": graph_ms["rmsnorm_fwd"] and round(
+                               fwd_bytes(M, N) / graph_ms["rmsnorm_fwd"] / 1e6, 1),
+                           "rmsnorm_bwd_ms": graph_ms["rmsnorm_bwd"] and round(graph_ms["rmsnorm_bwd"], 4),
+                           "rmsnorm_bwd_gbs": graph_ms["rmsnorm_bwd"] and round(
+                               bwd_bytes(M, N) / graph_ms["rmsnorm_bwd"] / 1e6, 1)}},
             "roofline": {"bound": "hbm", "kernel": fwd_kernel,
                          "achieved": round(fwd_gbs, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(fwd_gbs / peak, 4), "peak_source": peak_src,

@@ -88,23 +88,44 @@ class PeerAllReduce:
         import ctypes
         local = ctypes.c_void_p()
         handle = ctypes.create_string_buffer(_C.QB_PEER_HANDLE_BYTES)
-        with torch.cuda.device(self.device):
-            _C.check(lib.qb_peer_buffer_create(self.world, self.cap_cols, byref(local), handle),
-                     "peer_buffer_create")
-        self._local = local.value
+        self._local = None
         self._peers = [None] * self.world
-        self._peers[self.rank] = self._local
+        # A rank whose create or open fails still takes part in every collective of the set-up, so
+        # that all ranks learn of the failure together and raise together (no rank is left waiting).
+        error = None
+        try:
+            with torch.cuda.device(self.device):
+                _C.check(lib.qb_peer_buffer_create(self.world, self.cap_cols, byref(local), handle),
+                         "peer_buffer_create")
+            self._local = local.value
+            self._peers[self.rank] = self._local
+        except Exception as exc:
+            if self.world == 1:
+                raise
+            error = exc
         if self.world > 1:
             handles = [None] * self.world
-            dist.all_gather_object(handles, handle.raw, group=group)
-            with torch.cuda.device(self.device):
-                for r in range(self.world):
-                    if r == self.rank:
-                        continue
-                    peer = ctypes.c_void_p()
-                    _C.check(lib.qb_peer_buffer_open(handles[r], byref(peer)), "peer_buffer_open")
-                    self._peers[r] = peer.value
-            dist.barrier(group=group)  # every buffer is mapped everywhere before the first store
+            dist.all_gather_object(handles, handle.raw if error is None else None, group=group)
+            if error is None and all(h is not None for h in handles):
+                try:
+                    with torch.cuda.device(self.device):
+                        for r in range(self.world):
+                            if r == self.rank:
+                                continue
+                            peer = ctypes.c_void_p()
+                            _C.check(lib.qb_peer_buffer_open(handles[r], byref(peer)), "peer_buffer_open")
+                            self._peers[r] = peer.value
+                except Exception as exc:
+                    error = exc
+            elif error is None:
+                error = RuntimeError("a peer rank could not create its exchange buffer")
+            # also the barrier: every buffer is mapped everywhere before the first store
+            ok = torch.tensor([0 if error is not None else 1], device=self.device, dtype=torch.int32)
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+            if int(ok) == 0:
+                self._release()  # no kernel has run yet, and the all-reduce above was the barrier
+                raise RuntimeError(f"PeerAllReduce set-up failed on at least one rank "
+                                   f"(this rank: {error!r})")
 
     def reduce(self, partials, outs=None, outs_f32=None) -> None:
         """partials: one or two fp32 ``[P, cols]`` buffers of the same shape; outs / outs_f32:
@@ -177,15 +198,21 @@ class PeerAllReduce:
     def close(self) -> None:
         if self._local is None:
             return
-        lib = _C.lib()
         torch.cuda.synchronize(self.device)
         if self.world > 1:
             dist.barrier(group=self.group)  # nobody stores into a buffer that is being freed
+        self._release()
+
+    def _release(self) -> None:
+        """Unmaps the peers' buffers and frees this rank's; no collective (the caller has made sure
+        that no rank still stores into them)."""
+        lib = _C.lib()
         with torch.cuda.device(self.device):
             for r, ptr in enumerate(self._peers):
                 if r != self.rank and ptr is not None:
                     lib.qb_peer_buffer_close(ptr)
-            lib.qb_peer_buffer_destroy(self._local)
+            if self._local is not None:
+                lib.qb_peer_buffer_destroy(self._local)
         self._local = None
         self._peers = []
 
