@@ -179,6 +179,19 @@ def _best_of(fn, repeats, warmup=1):
     return best
 
 
+def cpu_model() -> str:
+    """Model name of the host CPU (first entry of /proc/cpuinfo), or the platform's answer."""
+    try:
+        with open("/proc/cpuinfo") as fh:
+            for line in fh:
+                if line.lower().startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or platform.machine()
+
+
 def cpu_baselines() -> dict:
     """The oracle on the host cores for every benchmark configuration: C1 and the headline C2 at
     full size, the others on a stated row slice (their fp32 upcasts need 4 - 17 GB per tensor at
@@ -188,11 +201,12 @@ def cpu_baselines() -> dict:
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
     used = torch.get_num_threads()
+    model = cpu_model()
     out = {}
 
     def rec(name, seconds, nbytes, sample):
         out[name] = {"value": round(nbytes / seconds / 1e9, 3), "unit": "GB/s", "cores": used,
-                     "kind": "port", "ms": round(seconds * 1e3, 2), "sample": sample}
+                     "kind": "port", "ms": round(seconds * 1e3, 2), "sample": sample, "cpu": model}
 
     # C1: RMSNorm forward fp32 [4096, 4096], exactly as stated
     d = oracle.make_config_inputs("c1")
@@ -259,7 +273,7 @@ def run_reference(args) -> None:
         "arm": "the reference's PyTorch CPU reference functions (rmsnorm_ref / rmsnorm_bwd_ref, "
                "restated in oracle/) on the host cores; one rank's workload (the CPU arm does not shard)",
         "cpu_baseline": {"value": val, "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
-                         "sample": f"each step = all {M_ROWS} rows, full N={N_COLS}"},
+                         "sample": f"each step = all {M_ROWS} rows, full N={N_COLS}", "cpu": cpu_model()},
         "e2e": {"value": val, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
     }
