@@ -1,7 +1,7 @@
 """Benchmark of the row-reduction hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--no-suite] [--no-e2e] [--only NAME ...]
+                    [--no-suite] [--no-e2e] [--no-graph] [--only NAME ...]
 
 A step is one pass of the headline workload -- RMSNorm forward + backward, bf16 [32768, 8192] with
 a residual (weight bf16, eps 1e-6) -- on every rank (weak scaling: each GPU owns its own 32768
@@ -407,7 +407,7 @@ def host_overhead(dev) -> dict:
     return res
 
 
-def suite(dev, peak, cpu) -> dict:
+def suite(dev, peak, cpu, no_graph=False) -> dict:
     """Every other kernel of the hot path at its benchmark configuration: median device ms of 20
     launches, GB/s of algorithmic bytes, the fraction of the measured copy peak, the kernel that
     ran, and the CPU oracle's figure where one was taken.  Outside the timed region."""
@@ -433,7 +433,7 @@ def suite(dev, peak, cpu) -> dict:
     def timed(name, fn, nbytes, iters=20):
         ms = time_kernel(fn, iters=iters)
         rec(name, ms, nbytes, _C.last_kernel())
-        ms_g = time_kernel_graph(fn)
+        ms_g = None if no_graph else time_kernel_graph(fn)
         if ms_g is not None:
             res[name]["cuda_graph"] = {"ms": round(ms_g, 4), "gbs": round(nbytes / ms_g / 1e6, 1),
                                        "protocol": "20 launches in one CUDA graph, median of 7 replays"}
@@ -916,7 +916,7 @@ def run_ours(args) -> None:
 
     # the same step and its two main kernels with the host launch path taken out (one GPU only)
     graph_ms = None
-    if world == 1:
+    if world == 1 and not args.no_graph:
         graph_ms = {
             "step": time_kernel_graph(lambda: step(False), launches=20),
             "rmsnorm_fwd": time_kernel_graph(
@@ -1090,7 +1090,7 @@ def run_ours(args) -> None:
             try:
                 del x, res, dout, out, res_out, dx
                 torch.cuda.empty_cache()
-                kernels.update(suite(dev, peak, cpu))
+                kernels.update(suite(dev, peak, cpu, args.no_graph))
                 kernels["host_us_per_call"] = host_overhead(dev)
             except Exception as exc:  # the headline line must still be printed
                 kernels["suite_error"] = repr(exc)
@@ -1185,6 +1185,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-suite", action="store_true", help="skip the per-kernel sweep of the other configurations")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="skip the CUDA-graph timings (keeps a profiler's launch list short)")
     ap.add_argument("--no-e2e", action="store_true",
                     help="skip the end-to-end leg (for profiler launch lists of the timed step alone)")
     ap.add_argument("--collective", default="peer", choices=["peer", "nccl", "none"],
