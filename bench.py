@@ -975,7 +975,7 @@ def run_ours(args) -> None:
         # quack.rmsnorm + autograd backward on a second, and the results return on a third, so that
         # the two PCIe directions and the kernels overlap.  The weight gradient accumulates in
         # weight.grad over the blocks, as autograd does for any micro-batched loop.
-        E2E_BLOCKS = 8
+        E2E_BLOCKS = args.e2e_blocks
         rows_blk = M // E2E_BLOCKS
         s_in, s_cmp, s_out = (torch.cuda.Stream(device=dev) for _ in range(3))
 
@@ -1045,7 +1045,7 @@ def run_ours(args) -> None:
         e2e = {"value": world * step_bytes / float(e2e_ms) / 1e6, "unit": "GB/s",
                "h2d_bytes_per_step": 3 * M * N * 2 + N * 2, "d2h_bytes_per_step": 2 * M * N * 2 + N * 2,
                "ms_per_step": float(e2e_ms),
-               "api": "quack.rmsnorm(x, w, residual=res) + backward through autograd on 8 row blocks; "
+               "api": f"quack.rmsnorm(x, w, residual=res) + backward through autograd on {E2E_BLOCKS} row blocks; "
                       "pinned host buffers; x, residual, dout, weight copied in on one stream, out, "
                       "dx (= dresidual), dw copied back on another, kernels on a third"}
         del hx, hres, hdout, h_out, h_dx
@@ -1185,6 +1185,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-suite", action="store_true", help="skip the per-kernel sweep of the other configurations")
+    ap.add_argument("--e2e-blocks", type=int, default=16,
+                    help="row blocks of the end-to-end leg (copies and kernels of different blocks overlap)")
     ap.add_argument("--no-graph", action="store_true",
                     help="skip the CUDA-graph timings (keeps a profiler's launch list short)")
     ap.add_argument("--no-e2e", action="store_true",
