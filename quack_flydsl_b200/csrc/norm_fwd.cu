@@ -121,6 +121,10 @@ norm_fwd_kernel(const NormFwdParams p) {
   }
   const int chunk0 = g.t;  // chunk k of this thread is slice chunk chunk0 + k * tpr
 
+  // Rows of one CTA may take different branches around a row reduction only if that reduction
+  // neither shuffles across rows (rows narrower than a warp) nor uses the CTA-wide barrier for a
+  // row group (see row_group_sync).
+  const bool ln_fast = LN && p.tpr >= 32 && (p.tpr == 32 || p.tpr == nthreads || nthreads <= 15 * p.tpr);
   const int64_t tile_stride = gridDim.x / p.cluster_n;
   int rit = 0;
   bool first = true;
@@ -181,40 +185,58 @@ norm_fwd_kernel(const NormFwdParams p) {
     float mean = 0.0f;
     float rstd;
     if constexpr (LN) {
-      float sv[VEC];
+      // Sum and sum of squares in ONE pass over the registers and one reduction.  var = E[x^2] -
+      // mean^2 loses (1 + mean^2 / var) ulps to cancellation, so it is only kept while the mean is
+      // small against the spread (mean^2 <= 4 var: below 1e-6 relative); any other row -- and any
+      // row with a NaN or infinity -- takes the centred second pass.  The choice is the same for
+      // all threads of a row; it may differ between the rows of a CTA only where the reduction
+      // does not synchronise threads of different rows (ln_fast), otherwise the rows of a warp
+      // or of the CTA decide together.
+      float sv[VEC], qv[VEC];
 #pragma unroll
-      for (int i = 0; i < VEC; ++i) sv[i] = 0.0f;
+      for (int i = 0; i < VEC; ++i) { sv[i] = 0.0f; qv[i] = 0.0f; }
 #pragma unroll
       for (int k = 0; k < K; ++k) {
         if constexpr (RAW) {
           float t[VEC];
           unpack_chunk<DT, VEC>(t, rx[k], a.x_dtype);
           vadd<VEC>(sv, sv, t);
+          vfma<VEC>(qv, t, t, qv);
         } else {
           vadd<VEC>(sv, sv, v[k]);
+          vfma<VEC>(qv, v[k], v[k], qv);
         }
       }
-      mean = row_reduce<SumOp, true>(make_float2(hsum<VEC>(sv), 0.f), g, scratch, 0, rit, p.timeouts).x * inv_n;
-      // sum (x - mean)^2; padding chunks hold zeros and get offset 0 instead of -mean
-      float qv[VEC];
-#pragma unroll
-      for (int i = 0; i < VEC; ++i) qv[i] = 0.0f;
-#pragma unroll
-      for (int k = 0; k < K; ++k) {
-        float d[VEC];
-        const float off = (k < nk) ? -mean : 0.0f;
-        if constexpr (RAW) {
-          float t[VEC];
-          forget_values(rx[k]);
-          unpack_chunk<DT, VEC>(t, rx[k], a.x_dtype);
-          vadd_s<VEC>(d, t, off);
-        } else {
-          vadd_s<VEC>(d, v[k], off);
-        }
-        vfma<VEC>(qv, d, d, qv);
+      const float2 sq =
+          row_reduce<SumOp, true>(make_float2(hsum<VEC>(sv), hsum<VEC>(qv)), g, scratch, 0, rit, p.timeouts);
+      mean = sq.x * inv_n;
+      float var = fmaf(-mean, mean, sq.y * inv_n);
+      bool exact = !(mean * mean <= 4.0f * var);
+      if (!ln_fast) {
+        // rows narrower than a warp (shuffle-only reductions): one choice per warp; row groups on
+        // the CTA-wide barrier: one choice per CTA
+        exact = (p.tpr < 32) ? (__any_sync(0xffffffffu, exact) != 0) : (__syncthreads_or(exact) != 0);
       }
-      const float var =
-          row_reduce<SumOp, true>(make_float2(hsum<VEC>(qv), 0.f), g, scratch, 1, rit, p.timeouts).x * inv_n;
+      if (exact) {
+        // sum (x - mean)^2; padding chunks hold zeros and get offset 0 instead of -mean
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) qv[i] = 0.0f;
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+          float d[VEC];
+          const float off = (k < nk) ? -mean : 0.0f;
+          if constexpr (RAW) {
+            float t[VEC];
+            forget_values(rx[k]);
+            unpack_chunk<DT, VEC>(t, rx[k], a.x_dtype);
+            vadd_s<VEC>(d, t, off);
+          } else {
+            vadd_s<VEC>(d, v[k], off);
+          }
+          vfma<VEC>(qv, d, d, qv);
+        }
+        var = row_reduce<SumOp, true>(make_float2(hsum<VEC>(qv), 0.f), g, scratch, 1, rit, p.timeouts).x * inv_n;
+      }
       rstd = rsqrtf(var + a.eps);
     } else {
       float qv[VEC];
