@@ -205,6 +205,42 @@ def test_norm_forward_streamed_long_rows(force, monkeypatch):
     torch.testing.assert_close(o.cpu(), oracle.layernorm_ref(x.cpu(), w.cpu(), eps=1e-5), atol=5e-3, rtol=1e-3)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("N", [64, 128, 256, 512, 768, 1024, 2048, 4096, 6144, 8192, 16384])
+def test_layernorm_statistics_one_pass_and_centred_rows_mixed(N, dtype):
+    """The register kernel takes sum and sum of squares in one pass and falls back to the centred
+    second pass for rows whose mean is large against their spread.  Rows of both kinds alternate
+    here, so that they meet inside one CTA and -- for rows narrower than a warp -- inside one
+    warp; constant rows (variance 0), an all-zero row and rows scaled far down are included.
+    rstd must hold rtol 1e-5 against the oracle on every row, whichever branch it took."""
+    M = 301
+    g = torch.Generator(device=DEV).manual_seed(N)
+    x = torch.randn(M, N, device=DEV, generator=g)
+    x[::3] += 50.0          # mean^2 >> var: centred pass
+    x[1::7] *= 1e-3         # tiny spread around 0: one pass
+    x[2::11] = x[2::11] * 1e-3 + 7.0   # tiny spread around 7: centred pass
+    x[5] = 3.0              # constant row
+    x[6] = 0.0              # zero row
+    x = x.to(dtype)
+    w = (1 + 0.1 * torch.randn(N, device=DEV, generator=g)).to(dtype)
+    b = (0.1 * torch.randn(N, device=DEV, generator=g)).to(dtype)
+    out = torch.empty_like(x)
+    rstd, mean = torch.empty(M, device=DEV), torch.empty(M, device=DEV)
+    rnm._rmsnorm_fwd(x, w, out, b, rstd, mean, None, None, 1e-5, True)
+    xc = x.cpu()
+    torch.testing.assert_close(mean.cpu(), oracle.layernorm_mean_ref(xc), atol=1e-6, rtol=1e-5)
+    torch.testing.assert_close(rstd.cpu(), oracle.layernorm_rstd_ref(xc, eps=1e-5), atol=0, rtol=1e-5)
+    ref = oracle.layernorm_ref(xc, w.cpu(), b.cpu(), eps=1e-5).float()
+    assert torch.isfinite(out.float()).all()
+    # rows with a tiny spread amplify the rounding of the mean by rstd (up to 316): compare the
+    # ordinary rows tightly and all rows against the bound that amplification allows
+    plain = torch.ones(M, dtype=torch.bool)
+    plain[1::7] = False; plain[2::11] = False; plain[5] = False; plain[6] = False
+    assert_close_to_oracle(out[plain.to(DEV)], ref[plain], dtype, atol={torch.float32: 1e-4}.get(dtype), what="out")
+    tol = 2e-3 if dtype == torch.float32 else 5e-2
+    assert float((out.cpu().float() - ref).abs().max()) <= tol * max(1.0, float(ref.abs().max()))
+
+
 def test_norm_forward_long_rows_residual_out_in_place():
     """residual_out may be the residual buffer itself (in-place residual stream update); long rows
     must then not take the kernel that reads the inputs a second time."""
