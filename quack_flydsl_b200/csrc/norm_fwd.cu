@@ -482,8 +482,22 @@ extern "C" int qb_norm_fwd(const qb_norm_fwd_args* args, qb_stream_t stream) {
   // runs 6.08 TB/s as one 128-thread CTA of 8 chunks per thread against 5.57 TB/s the other way;
   // LayerNorm, with its second pass over the registers, keeps 16 chunks: 5.88 against 4.40 TB/s.)
   const bool one_cta_row = raw && !a.is_layernorm && a.N * host_dtype_bytes(a.x_dtype) == 16384;
-  const int k_target = (raw && !one_cta_row) ? 16 : 8;
-  const int default_threads = raw && a.N >= 6144 && !one_cta_row ? 256 : 128;
+  int k_target = (raw && !one_cta_row) ? 16 : 8;
+  int default_threads = raw && a.N >= 6144 && !one_cta_row ? 256 : 128;
+  // RMSNorm rows of 4 - 8 KB (16-bit hidden sizes 2048 ... 4096): half the chunks per thread and
+  // twice the threads per row.  Measured (bf16, 512 MiB per tensor, with residual / without):
+  // N = 4096 6.06 -> 6.39 / 5.63 -> 6.16 TB/s, N = 2048 5.82 -> 6.39 / 5.60 -> 6.08.
+  // Only rows that fill such a tile exactly (N = 3072 would leave a quarter of it empty: -2 %).
+  const int64_t row_bytes_x = a.N * host_dtype_bytes(a.x_dtype);
+  if (!a.is_layernorm && uniform && vec == 8 && row_bytes_x >= 4096 && row_bytes_x <= 8192) {
+    const int kt = raw ? 8 : 4;
+    const int64_t chunks = a.N / vec;
+    const int64_t tpr_c = chunks / kt;
+    if (chunks % kt == 0 && (tpr_c & (tpr_c - 1)) == 0) {
+      k_target = kt;
+      if (raw && row_bytes_x >= 6144) default_threads = 256;
+    }
+  }
   // RMSNorm rows that split evenly over a cluster stay on the register kernel: with the st.async
   // exchange it beats the two-pass kernel at every long row measured (bf16, 512 MiB per tensor,
   // without / with residual: N = 65536 5.36 / 6.04 against 4.91 / 5.65 TB/s, N = 131072 5.13 /
