@@ -484,12 +484,13 @@ extern "C" int qb_norm_fwd(const qb_norm_fwd_args* args, qb_stream_t stream) {
   const bool one_cta_row = raw && !a.is_layernorm && a.N * host_dtype_bytes(a.x_dtype) == 16384;
   int k_target = (raw && !one_cta_row) ? 16 : 8;
   int default_threads = raw && a.N >= 6144 && !one_cta_row ? 256 : 128;
-  // RMSNorm rows of 4 - 8 KB (16-bit hidden sizes 2048 ... 4096): half the chunks per thread and
+  // RMSNorm rows of 2 - 8 KB (16-bit hidden sizes 1024 ... 4096): half the chunks per thread and
   // twice the threads per row.  Measured (bf16, 512 MiB per tensor, with residual / without):
-  // N = 4096 6.06 -> 6.39 / 5.63 -> 6.16 TB/s, N = 2048 5.82 -> 6.39 / 5.60 -> 6.08.
+  // N = 4096 6.06 -> 6.39 / 5.63 -> 6.16 TB/s, N = 2048 5.82 -> 6.39 / 5.60 -> 6.08,
+  // N = 1024 5.97 -> 6.07 / 5.79 -> 6.12.
   // Only rows that fill such a tile exactly (N = 3072 would leave a quarter of it empty: -2 %).
   const int64_t row_bytes_x = a.N * host_dtype_bytes(a.x_dtype);
-  if (!a.is_layernorm && uniform && vec == 8 && row_bytes_x >= 4096 && row_bytes_x <= 8192) {
+  if (!a.is_layernorm && uniform && vec == 8 && row_bytes_x >= 2048 && row_bytes_x <= 8192) {
     const int kt = raw ? 8 : 4;
     const int64_t chunks = a.N / vec;
     const int64_t tpr_c = chunks / kt;
