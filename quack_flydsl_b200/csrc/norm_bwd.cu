@@ -410,6 +410,26 @@ static int launch_norm_bwd_k(const NormBwdParams& p, dim3 grid, int threads, siz
 template <int DT, int VEC>
 static int launch_norm_bwd_v(const NormBwdParams& p, int K, dim3 grid, int threads, size_t smem,
                              cudaStream_t st) {
+  // Rows whose chunk count is 3, 5, 6 or 7 times the threads of a row (16-bit hidden sizes such
+  // as 3072, 5120, 7168) would fill only part of the power-of-two tile: every thread would carry
+  // zeroed padding chunks through both passes.  Kernels with exactly that many chunks per thread
+  // serve them (single-CTA rows, uniform 16-bit dtypes).  Measured, RMSNorm backward bf16, 512 MiB
+  // per tensor: N = 5120 4.40 -> 5.21 TB/s, 10240 3.95 -> 5.11, 2560 4.39 -> 5.13, 3072 5.10 -> 5.45,
+  // 1536 5.19 -> 5.96; dx is bit-identical to the padded kernel's.
+  if constexpr (DT != kDynDT && VEC == 8) {
+    const int64_t nchunks = p.cols_per_cta / VEC;
+    if (p.cluster_n == 1 && !(p.a.cfg.flags & 1) && p.a.N == p.cols_per_cta && nchunks % p.tpr == 0) {
+      const int64_t ku = nchunks / p.tpr;
+      if (K == 4 && ku == 3) return launch_norm_bwd_c<DT, VEC, 3, 0, false>(p, grid, threads, smem, st);
+      if (K == 8 && ku == 5) return launch_norm_bwd_c<DT, VEC, 5, 0, false>(p, grid, threads, smem, st);
+      if (K == 8 && ku == 6) return launch_norm_bwd_c<DT, VEC, 6, 0, false>(p, grid, threads, smem, st);
+      // (7 of 8: only where the 8-chunk kernel has no compile-time geometry -- with it, N = 7168
+      // runs 5.73 against 5.55 TB/s; without, N = 14336 5.05 against 5.58)
+      const bool has_static_geometry = threads == 128 && (p.tpr == 64 || p.tpr == 128);
+      if (K == 8 && ku == 7 && !has_static_geometry)
+        return launch_norm_bwd_c<DT, VEC, 7, 0, false>(p, grid, threads, smem, st);
+    }
+  }
   switch (K) {
     case 1: return launch_norm_bwd_k<DT, VEC, 1>(p, grid, threads, smem, st);
     case 2: return launch_norm_bwd_k<DT, VEC, 2>(p, grid, threads, smem, st);

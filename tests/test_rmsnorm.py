@@ -426,3 +426,50 @@ def test_rmsnorm_compile_2d_then_4d():
     torch.testing.assert_close(r4.grad.float().cpu(), rr.grad, atol=1e-1, rtol=1e-2)
     torch.testing.assert_close(w2.grad.cpu(), wr.grad, atol=2e-2 * 32 ** 0.5, rtol=1e-2)
     torch.testing.assert_close(b2.grad.cpu(), br.grad, atol=2e-2 * 32 ** 0.5, rtol=1e-2)
+
+
+@pytest.mark.parametrize("is_layernorm", [False, True])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("N", [1536, 2560, 3072, 3584, 5120, 7168, 10240, 14336])
+def test_norm_backward_rows_of_three_five_six_seven_chunks(N, dtype, is_layernorm, monkeypatch):
+    """Hidden sizes whose 16-byte chunk count is 3, 5, 6 or 7 times the threads of a row are served
+    by backward kernels with exactly that many chunks per thread (no padding chunks).  dx against
+    the oracle, dw / db against its column sums, for several rows per CTA and a single row; the
+    padded 8-chunk kernel (flag bit 1) must give bit-identical dx."""
+    from quack_flydsl_b200 import _C
+    from quack_flydsl_b200.rmsnorm_config import get_sm_count
+
+    g = torch.Generator(device=DEV).manual_seed(N)
+    for M in (333, 1):
+        x = (0.3 + torch.randn(M, N, device=DEV, generator=g)).to(dtype)
+        w = (1 + 0.1 * torch.randn(N, device=DEV, generator=g)).to(dtype)
+        dout = torch.randn(M, N, device=DEV, generator=g).to(dtype)
+        xc = x.cpu()
+        if is_layernorm:
+            rstd_c, mean_c = oracle.layernorm_rstd_ref(xc, eps=1e-5), oracle.layernorm_mean_ref(xc)
+            dx_ref, dw_ref, db_ref = oracle.layernorm_bwd_ref(xc, w.cpu(), dout.cpu(), rstd_c, mean_c)
+        else:
+            rstd_c, mean_c = oracle.rmsnorm_rstd_ref(xc, eps=1e-6), None
+            dx_ref, dw_ref, db_ref = oracle.rmsnorm_bwd_ref(xc, w.cpu(), dout.cpu(), rstd_c)
+        rstd = rstd_c.to(DEV)
+        mean = mean_c.to(DEV) if is_layernorm else None
+        P = get_sm_count(N, torch.device(DEV), dtype)
+        results = {}
+        for padded in (False, True):
+            dx = torch.full_like(x, 7.0)
+            dwp = torch.full((P, N), 7.0, device=DEV)
+            dbp = torch.full((P, N), 7.0, device=DEV) if is_layernorm else None
+            if padded:
+                monkeypatch.setenv("QUACK_B200_CFG", "norm_bwd:0:0:0:0:0:1")
+            else:
+                monkeypatch.delenv("QUACK_B200_CFG", raising=False)
+            rn._rmsnorm_bwd(x, w, dout, rstd, dx, dwp, dbp, None, None, P, mean, is_layernorm)
+            results[padded] = (dx, dwp.sum(0), dbp.sum(0) if is_layernorm else None, _C.last_kernel())
+        monkeypatch.delenv("QUACK_B200_CFG", raising=False)
+        dx, dw, db, kernel = results[False]
+        assert torch.equal(dx, results[True][0]), (kernel, results[True][3])
+        assert_close_to_oracle(dx, dx_ref, dtype, max_ulp=None, what="dx")
+        sum_atol = 1e-3 * (M ** 0.5) * 4
+        torch.testing.assert_close(dw.cpu(), dw_ref.float(), atol=sum_atol, rtol=1e-2)
+        if is_layernorm:
+            torch.testing.assert_close(db.cpu(), db_ref.float(), atol=sum_atol, rtol=1e-2)
