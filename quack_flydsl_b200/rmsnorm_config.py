@@ -34,8 +34,16 @@ class RmsNormFwdConfig:
         up to 16 chunks per thread and 256-thread CTAs from N = 6144, which this value does not
         describe; ``qb_last_kernel`` names the instantiation that actually ran."""
         vec = 128 // dtype_width
+        k_target = 8
+        # RMSNorm rows of 2 - 8 KB of 16-bit elements that fill a power-of-two tile exactly
+        # (hidden sizes 1024, 2048, 4096): half the chunks per thread, twice the threads per row
+        row_bytes = N * dtype_width // 8
+        if not is_layernorm and vec == 8 and 2048 <= row_bytes <= 8192 and N % (vec * 4) == 0:
+            tpr_c = N // (vec * 4)
+            if tpr_c & (tpr_c - 1) == 0:
+                k_target = 4
         threads, tpr, cluster_n = _plan(N, vec, pref_elems=16384 if vec == 8 else 8192,
-                                        k_target=8, caps=(64, 32, 16), default_threads=128)
+                                        k_target=k_target, caps=(64, 32, 16), default_threads=128)
         return cls(num_threads=threads, threads_per_row=tpr, cluster_n=cluster_n)
 
 

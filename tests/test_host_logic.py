@@ -124,6 +124,13 @@ def test_config_dataclasses_and_search_spaces():
     # short rows: several rows per CTA
     hs = RmsNormFwdConfig.from_analytical_heuristic(256, 16)
     assert hs.threads_per_row < hs.num_threads
+    # RMSNorm at hidden sizes 1024 ... 4096 (16-bit, with residual): four chunks per thread
+    for n, tpr in ((4096, 128), (2048, 64), (1024, 32)):
+        hf = RmsNormFwdConfig.from_analytical_heuristic(n, 16)
+        assert (hf.num_threads, hf.threads_per_row, hf.cluster_n) == (128, tpr, 1), (n, hf)
+    # LayerNorm and rows that do not fill such a tile keep eight chunks per thread
+    assert RmsNormFwdConfig.from_analytical_heuristic(4096, 16, is_layernorm=True).threads_per_row == 64
+    assert RmsNormFwdConfig.from_analytical_heuristic(3072, 16).threads_per_row == 64
 
 
 def test_selection_cache_counts_specialisations():
